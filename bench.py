@@ -1,0 +1,281 @@
+"""DCC-KV layer prefill benchmark: tokens/s of the full 128K-context layer.
+
+Workload: 131072 tokens as 8 blocks of 16384, 32 query / 8 KV heads,
+head_dim 128, bf16, compact budget 1024 per (source, destination) edge,
+destination window 2048 queries per query head, M = 64 representative
+queries, d_p = 32.  A step is one forward of the layer over the whole
+context: pooling + 28 x 8 compact builds + local causal attention +
+compact attention with logit bias + online-softmax merge.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl reference]
+
+N = 1 runs the 8 logical blocks on one GPU.  ``--impl reference`` times the
+FP64 CPU oracle (a restatement of the reference path) on a bounded sample
+of the same workload and extrapolates to the full layer.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_BLOCKS, BLOCK_LEN, HQ, HKV, D = 8, 16384, 32, 8, 128
+BUDGET, WINDOW, M_REPR, DP = 1024, 2048, 64, 32
+TOKENS = N_BLOCKS * BLOCK_LEN
+METRIC = "DCC-KV layer prefill tokens/s at 128K ctx"
+WORKLOAD = {"workload": "dcc_kv_sync_layer_128k", "context_tokens": TOKENS, "blocks": N_BLOCKS,
+            "block_len": BLOCK_LEN, "q_heads": HQ, "kv_heads": HKV, "head_dim": D, "budget": BUDGET,
+            "window": WINDOW, "repr_queries": M_REPR, "projection_dim": DP,
+            "l2": "inputs larger than L2 (q 1 GiB, k/v 256 MiB each)"}
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], p["bf16_tflops_sustained"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, 1400.0, "fallback"
+
+
+def causal_attention_flops():
+    """Algorithmic FLOPs of one step's attention: local causal (L(L+1)/2 pairs
+    per head and block) and compact (block r sees r * BUDGET keys), 4 d per pair."""
+    local = N_BLOCKS * HQ * (BLOCK_LEN * (BLOCK_LEN + 1) // 2) * 4 * D
+    compact = sum(HQ * BLOCK_LEN * r * BUDGET * 4 * D for r in range(N_BLOCKS))
+    return local, compact
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.path = None
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [x.strip() for x in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        finally:
+            if self.path:
+                os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def dist_env():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return ws, rank, local
+
+
+# ---------------------------------------------------------------------------
+# reference arm / CPU baseline: the FP64 oracle on a bounded sample
+# ---------------------------------------------------------------------------
+def cpu_sample(seconds_budget: float = 20.0):
+    """Time the oracle on (a) one full-size edge build for one KV head and
+    (b) attention of sampled query rows against full-size blocks, then
+    extrapolate to the layer: 28 edges x 8 KV heads of builds and every
+    (query row, visible key) pair of the local and compact attention."""
+    import numpy as np
+    from oracle import dcc_kv_oracle as orc
+    from dcc_kv_b200.workloads import gqa_block
+
+    q, k, v = gqa_block(HQ, HKV, BLOCK_LEN, D, seed=1000, device="cpu")
+    q1, _, _ = gqa_block(HQ, HKV, BLOCK_LEN, D, seed=1001, device="cpu")
+    k64, v64 = k[0].double().numpy(), v[0].double().numpy()
+    dq = np.concatenate([q1[j, :WINDOW].double().numpy() for j in range(4)])
+    t0 = time.perf_counter()
+    qh, _ = orc.select_representative_queries(dq, M_REPR, DP)
+    t_pool = time.perf_counter() - t0
+    t0 = time.perf_counter()
+    c = orc.build_compact_kv_from_repr(k64, v64, qh, BUDGET)
+    t_build = time.perf_counter() - t0
+    rows = 64
+    qs = q[0, -rows:].double().numpy()
+    t0 = time.perf_counter()
+    orc.attention_partial(qs, k64, v64, positions=np.arange(BLOCK_LEN - rows, BLOCK_LEN))
+    orc.attention_partial(qs, c.keys, c.values, bias=c.logit_bias)
+    t_attn = time.perf_counter() - t0
+    pairs_sample = rows * (BLOCK_LEN + BUDGET)
+    local_pairs = N_BLOCKS * HQ * BLOCK_LEN * (BLOCK_LEN + 1) // 2
+    compact_pairs = sum(HQ * BLOCK_LEN * r * BUDGET for r in range(N_BLOCKS))
+    n_edges = N_BLOCKS * (N_BLOCKS - 1) // 2
+    total = ((N_BLOCKS - 1) * HKV * t_pool + n_edges * HKV * t_build
+             + (local_pairs + compact_pairs) * t_attn / pairs_sample)
+    sample = (f"one KV head: FPS over {4 * WINDOW} queries ({t_pool:.2f}s) + one edge build "
+              f"L_s={BLOCK_LEN} B={BUDGET} ({t_build:.2f}s) + {rows} query rows x {BLOCK_LEN + BUDGET} keys "
+              f"({t_attn:.2f}s); extrapolated to {n_edges * HKV} builds and "
+              f"{local_pairs + compact_pairs:.3e} (row, key) pairs")
+    return total, sample
+
+
+def run_reference(args):
+    ws, rank, _ = dist_env()
+    if rank != 0:
+        return
+    cores = os.cpu_count() or 1
+    torch.set_num_threads(cores)
+    for _ in range(args.warmup):
+        cpu_sample()
+    times, sample = [], ""
+    for _ in range(args.steps):
+        t, sample = cpu_sample()
+        times.append(t)
+    mean_t = sum(times) / len(times)
+    value = TOKENS / mean_t
+    line = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": mean_t * 1e3, "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f64", "data": "synthetic (seeded, bf16-valued inputs)",
+            "config": dict(WORKLOAD, parallelism="cpu"), "impl": "reference",
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# GPU arm
+# ---------------------------------------------------------------------------
+def run_gpu(args):
+    import dcc_kv_b200 as dk
+    from dcc_kv_b200.workloads import layer_inputs
+
+    ws, rank, local = dist_env()
+    if ws > 1:
+        from dcc_kv_b200.dist_layer import run_distributed_bench
+        return run_distributed_bench(args)
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    q, k, v = layer_inputs(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, device="cuda")
+    layer = dk.DccKvSyncLayer(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    for _ in range(max(args.warmup, 3)):
+        layer(q, k, v)
+    torch.cuda.synchronize()
+    # device-timed region: whole steps, plus the local-attention launch alone
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    attn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(args.steps)]
+    layer.timing_events = attn_ev
+    with ClockSampler(torch.cuda.current_device()) as clk:
+        torch.cuda.synchronize()
+        for i in range(args.steps):
+            ev[i][0].record(stream)
+            layer.timing_index = i
+            layer(q, k, v)
+            ev[i][1].record(stream)
+        torch.cuda.synchronize()
+    layer.timing_events = None
+    step_ms = [a.elapsed_time(b) for a, b in ev]
+    attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
+    ms = sum(step_ms) / len(step_ms)
+    clocks = clk.summary()
+    # end to end through the public API: pinned host inputs in, output back to host
+    hq_, hk_, hv_ = (t.cpu().pin_memory() for t in (q, k, v))
+    out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    dq, dk_, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    for i in range(args.steps + 1):
+        if i > 0:
+            e2e_ev[i - 1][0].record(stream)
+        dq.copy_(hq_, non_blocking=True)
+        dk_.copy_(hk_, non_blocking=True)
+        dv.copy_(hv_, non_blocking=True)
+        out = layer(dq, dk_, dv)
+        out_host.copy_(out, non_blocking=True)
+        if i > 0:
+            e2e_ev[i - 1][1].record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev) / args.steps
+    hbm, tf_burst, tf_sust, src = peaks()
+    local_flops, compact_flops = causal_attention_flops()
+    a_ms = sum(attn_ms) / len(attn_ms)
+    achieved = local_flops / (a_ms * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": TOKENS / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1), 4 outlier channels x8 per KV head)",
+        "config": dict(WORKLOAD, parallelism="single GPU, 8 logical blocks"),
+        "e2e": {"value": TOKENS / (e2e_ms * 1e-3), "unit": "tokens/s",
+                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (q, k, v)),
+                "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
+        "gpu_launches": layer.launches_per_forward() * args.steps,
+        "roofline": {"kernel": "local causal attention (all 8 blocks, one launch)", "bound": "tensor",
+                     "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust,
+                     "peak_source": f"{src} bf16 sustained", "traffic": None,
+                     "algorithmic_flops": local_flops, "ms_per_launch": a_ms},
+        "clocks": clocks,
+    }
+    if args.cpu_baseline:
+        cores = os.cpu_count() or 1
+        torch.set_num_threads(cores)
+        t, sample = cpu_sample()
+        line["cpu_baseline"] = {"value": TOKENS / t, "unit": "tokens/s", "cores": cores, "kind": "port",
+                                "sample": sample}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,42 @@
+"""Helpers shared by the GPU parity tests."""
+from __future__ import annotations
+
+import os
+
+import numpy as np
+import torch
+
+from conftest import GOLDEN
+
+
+def dev():
+    return torch.device("cuda", 0)
+
+
+def golden(name):
+    return np.load(os.path.join(GOLDEN, name))
+
+
+def to_gpu(a, dtype):
+    return torch.as_tensor(np.asarray(a, dtype=np.float64)).to(dtype).to(dev())
+
+
+def np64(t):
+    return t.detach().double().cpu().numpy()
+
+
+def rel_err(got, want) -> float:
+    """max |got - want| / max |want|  (the relative tolerance used throughout)."""
+    got = np.asarray(got, dtype=np.float64)
+    want = np.asarray(want, dtype=np.float64)
+    return float(np.abs(got - want).max() / max(np.abs(want).max(), 1e-300))
+
+
+def build_inputs(f, name):
+    if name == "build_cfg1.npz":
+        g = torch.Generator().manual_seed(0)
+        K = torch.randn(4096, 128, generator=g, dtype=torch.float64).numpy()
+        V = torch.randn(4096, 128, generator=g, dtype=torch.float64).numpy()
+        Q = torch.randn(512, 128, generator=g, dtype=torch.float64).numpy()
+        return K, V, Q
+    return f["K"].astype(np.float64), f["V"].astype(np.float64), f["Q"].astype(np.float64)

@@ -1,0 +1,124 @@
+"""GPU parity of the destination side: segmented biased attention, the
+online-softmax kernels and the P-way LSE merge, against the oracle and the
+reference's golden vectors.
+
+Bars: float32 / float64 paths within 1e-4 relative (FP64 accumulation lands
+near 1e-7); bf16 inputs within 2e-2 relative on attention outputs.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import dcc_kv_b200 as dk
+from oracle import dcc_kv_oracle as orc
+
+from gpu_util import dev, golden, np64, rel_err, to_gpu
+
+pytestmark = pytest.mark.gpu
+
+
+def test_online_softmax_golden():
+    f = golden("online_softmax.npz")
+    d64 = torch.float64
+    s1 = dk.online_softmax_from_attention(to_gpu(f["logits1"], d64), to_gpu(f["values1"], d64))
+    s2 = dk.online_softmax_from_attention(to_gpu(f["logits2"], d64), to_gpu(f["values2"], d64),
+                                          logit_bias=to_gpu(f["bias"], d64))
+    for st, keys in ((s1, ("m1", "l1", "o1")), (s2, ("m2", "l2", "o2"))):
+        for got, k in zip((st.m, st.l, st.o), keys):
+            assert rel_err(np64(got), f[k]) < 1e-13
+    m = dk.merge_softmax_states(s1, s2)
+    for got, k in zip((m.m, m.l, m.o), ("m", "l", "o")):
+        assert rel_err(np64(got), f[k]) < 1e-13
+    # single-row form, as the reference calls it
+    one = dk.online_softmax_from_attention(to_gpu(f["logits1"][0], d64), to_gpu(f["values1"], d64))
+    assert one.o.shape == (f["values1"].shape[1],)
+    assert abs(float(one.m) - f["m1"][0]) < 1e-13
+
+
+def test_reference_kats():
+    """The reference's own online-softmax KATs (tests/test_dist_equivalence.py:45-119)."""
+    d = dev()
+    logits = torch.tensor([1.0, 2.0, 3.0], device=d)
+    values = torch.tensor([[1.0, 1.0], [2.0, 2.0], [3.0, 3.0]], device=d)
+    st = dk.online_softmax_from_attention(logits, values)
+    assert torch.allclose(st.o / st.l, torch.softmax(logits, -1) @ values, atol=1e-6)
+    s1 = dk.online_softmax_from_attention(torch.tensor([1.0, 2.0], device=d), torch.tensor([[1.0], [2.0]], device=d))
+    s2 = dk.online_softmax_from_attention(torch.tensor([3.0, 4.0], device=d), torch.tensor([[3.0], [4.0]], device=d))
+    full = dk.online_softmax_from_attention(torch.tensor([1.0, 2.0, 3.0, 4.0], device=d),
+                                            torch.tensor([[1.0], [2.0], [3.0], [4.0]], device=d))
+    mg = dk.merge_softmax_states(s1, s2)
+    assert torch.allclose(mg.o / mg.l, full.o / full.l, atol=1e-6)
+    bias = torch.tensor([0.0, 1.0, -1.0], device=d)
+    a = dk.online_softmax_from_attention(logits, values[:, :1], logit_bias=bias)
+    b = dk.online_softmax_from_attention(logits + bias, values[:, :1])
+    assert torch.allclose(a.m, b.m) and torch.allclose(a.l, b.l) and torch.allclose(a.o, b.o)
+    g = torch.Generator().manual_seed(0)
+    assert dk.verify_order_invariance([])
+    same_d = []
+    for _ in range(8):
+        n = int(torch.randint(4, 32, (1,), generator=g))
+        same_d.append(dk.online_softmax_from_attention(torch.randn(n, generator=g).to(d), torch.randn(n, 8, generator=g).to(d)))
+    assert dk.verify_order_invariance(same_d, n_trials=20, seed=42)
+
+
+@pytest.mark.parametrize("dtype,n_parts,dim", [(torch.bfloat16, 8, 128), (torch.bfloat16, 2, 128),
+                                               (torch.float32, 3, 64), (torch.float32, 5, 33),
+                                               (torch.float64, 4, 16)])
+def test_merge_lse(dtype, n_parts, dim):
+    g = torch.Generator().manual_seed(n_parts * 100 + dim)
+    outs = [torch.randn(4, 257, dim, generator=g, dtype=torch.float64) for _ in range(n_parts)]
+    lses = [torch.randn(4, 257, generator=g, dtype=torch.float64) * 4 for _ in range(n_parts)]
+    lses[0][0, :5] = -float("inf")  # an empty partial contributes nothing
+    o, lse = dk.merge_lse([x.to(dtype).to(dev()) for x in outs], [x.float().to(dev()) for x in lses])
+    ro = [x.to(dtype).double().numpy() for x in outs]
+    rl = [x.float().double().numpy() for x in lses]
+    want_o, want_l = orc.merge_lse(ro, rl)
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+    assert rel_err(np64(o), want_o) < tol
+    assert rel_err(np64(lse), want_l) < 1e-5
+
+
+def _attn_case(dtype, hq, hkv, lq, d, segs, causal, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(hq, lq, d, generator=g, dtype=torch.float64)
+    segments = []
+    for n, with_bias in segs:
+        k = torch.randn(hkv, n, d, generator=g, dtype=torch.float64)
+        v = torch.randn(hkv, n, d, generator=g, dtype=torch.float64)
+        b = torch.randn(hkv, n, generator=g, dtype=torch.float64) * 3 if with_bias else None
+        segments.append((k, v, b))
+    qd = q.to(dtype)
+    o, lse = dk.attention(qd.to(dev()), [(k.to(dtype).to(dev()), v.to(dtype).to(dev()),
+                                          None if b is None else b.float().to(dev())) for k, v, b in segments],
+                          causal=causal)
+    torch.cuda.synchronize()
+    grp = hq // hkv
+    for h in range(hq):
+        qh = qd[h].double().numpy()
+        parts = []
+        for i, (k, v, b) in enumerate(segments):
+            kk = k[h // grp].to(dtype).double().numpy()
+            vv = v[h // grp].to(dtype).double().numpy()
+            bb = None if b is None else b[h // grp].float().double().numpy()
+            pos = np.arange(lq) if (causal and i == 0) else None
+            parts.append(orc.attention_partial(qh, kk, vv, bias=bb, positions=pos))
+        want_o, want_l = orc.merge_lse([p[0] for p in parts], [p[1] for p in parts])
+        tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+        assert rel_err(np64(o[h]), want_o) < tol, h
+        assert rel_err(np64(lse[h]), want_l) < (1e-2 if dtype == torch.bfloat16 else 1e-5)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_attention_local_causal(dtype):
+    _attn_case(dtype, 8, 2, 300, 128, [(300, False)], True, 1)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_attention_biased_segments(dtype):
+    _attn_case(dtype, 4, 4, 129, 128, [(77, True), (64, True), (200, True)], False, 2)
+
+
+def test_attention_small_head_dim_f32():
+    _attn_case(torch.float32, 4, 2, 50, 32, [(50, False), (17, True)], True, 3)
