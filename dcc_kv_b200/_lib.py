@@ -89,6 +89,8 @@ SIGNATURES = {
     "dcc_build_compact_kv_workspace": (_SZ, [_I64, _I64, _I, _I, _I, _I, _I, _I]),
     "dcc_build_compact_kv": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _I, _I, _I, _D, _D, C.c_uint64, _I,
                                   _P, _P, _P, _P, _P, _P, _SZ, _P]),
+    "dcc_build_compact_kv_noalloc": (_I, [_P, _P, _P, _I64, _I64, _I, _I, _I, _I, _I, _D, _D, C.c_uint64, _I,
+                                          _P, _P, _P, _P, _P, _P]),
     "dcc_stage_workspace_bytes": (_SZ, [_I64, _I, _I, _I, _I, _I]),
     "dcc_select_topk_keys": (_I, [_P, _P, _I64, _I, _I, _I, _I, _P, _P, _P, _SZ, _P]),
     "dcc_fit_logit_bias": (_I, [_P, _P, _P, _I, _I, _I, _D, _I, _P, _P, _SZ, _P]),

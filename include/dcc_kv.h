@@ -124,6 +124,29 @@ int dcc_build_compact_kv(const void* source_keys, const void* source_values,
                          void* out_values, int64_t* out_selected_indices, int64_t* out_repr_idx,
                          void* workspace, size_t workspace_bytes, void* stream);
 
+/* No counterpart in the reference.  The single-head build above for callers
+ * that cannot call cudaMalloc: a plugin inside a host application that owns
+ * all device memory through its own fixed pool, or a latency-critical path
+ * where an allocation could fail or stall.  Same arguments and outputs as
+ * dcc_build_compact_kv without the workspace; the scratch is a fixed
+ * DCC_NOALLOC_SCRATCH_BYTES (16 MiB) device array inside the library, held
+ * by every GPU that loads it until the process exits.  Problems whose
+ * dcc_build_compact_kv_workspace() exceeds that size are rejected with
+ * DCC_ERR_UNSUPPORTED.  The first call on a device looks up the array's
+ * address (cudaGetSymbolAddress); make that first call before any stream
+ * capture.  All calls share the one array and nothing in it has to start at
+ * zero: calls that overlap on the GPU (other streams, other threads) race,
+ * so serialise them. */
+#define DCC_NOALLOC_SCRATCH_BYTES (16u << 20)
+int dcc_build_compact_kv_noalloc(const void* source_keys, const void* source_values,
+                                 const void* destination_queries, int64_t L_s, int64_t L_r,
+                                 int head_dim, int value_dim, int budget,
+                                 int num_representative_queries, int projection_dim,
+                                 double lambda_beta, double lambda_value, uint64_t seed, int dtype,
+                                 void* out_keys, void* out_bias, void* out_values,
+                                 int64_t* out_selected_indices, int64_t* out_repr_idx,
+                                 void* stream);
+
 /* ---- stage kernels exposed for the per-function API -----------------------
  * Scratch for the three single-problem stage entry points below. */
 size_t dcc_stage_workspace_bytes(int64_t L_s, int M, int budget, int head_dim, int value_dim, int dtype);
