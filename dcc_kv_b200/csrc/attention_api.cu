@@ -24,7 +24,7 @@ extern "C" int dcc_attention_fwd(const dcc_attn_problem* problems, int n_problem
     if (p.q_row_stride < head_dim || p.o_row_stride < head_dim)
       return fail(DCC_ERR_SHAPE, "attention_fwd: row stride smaller than head_dim");
     mma = mma && aligned16(p.q) && aligned16(p.o) && p.q_row_stride % 8 == 0 &&
-          p.q_head_stride % 8 == 0;
+          p.q_head_stride % 8 == 0 && p.o_row_stride % 8 == 0 && p.o_head_stride % 8 == 0;
     for (int s = 0; s < p.n_seg; ++s) {
       const dcc_kv_segment& g = p.seg[s];
       if (!g.k || !g.v || g.len < 0 || g.row_stride < head_dim)
@@ -36,6 +36,11 @@ extern "C" int dcc_attention_fwd(const dcc_attn_problem* problems, int n_problem
   if (n_problems == 0) return DCC_OK;
   AttnParams prm{n_q_heads, n_kv_heads, n_q_heads / n_kv_heads, head_dim, scale};
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (mma) {  // bf16, d 128, 16-byte aligned rows: the tcgen05 kernel when the shape allows
+    bool tc = true;
+    for (int i = 0; i < n_problems; ++i) tc = tc && attn_tc05_supported(problems[i], prm);
+    if (tc) return launch_attn_tc05(problems, n_problems, prm, st);
+  }
   AttnBatch b{};
   int64_t max_lq = 0;
   auto flush = [&]() -> int {

@@ -227,6 +227,10 @@ typedef struct dcc_attn_problem {
 
 int dcc_attention_fwd(const dcc_attn_problem* problems, int n_problems, int n_q_heads,
                       int n_kv_heads, int head_dim, double scale, int dtype, void* stream);
+/* Synchronises the current device and reports whether a bounded device-side
+ * wait of the tcgen05 attention kernel expired since the last clear
+ * (DCC_ERR_TIMEOUT), clearing the flag when `clear` is non-zero. */
+int dcc_device_error_status(int clear);
 
 /* ---- online softmax ------------------------------------------------------
  * online_softmax_from_attention (online_softmax.py:52-89), batched: logits

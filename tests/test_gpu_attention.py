@@ -12,6 +12,7 @@ import pytest
 import torch
 
 import dcc_kv_b200 as dk
+from dcc_kv_b200 import _lib as L
 from oracle import dcc_kv_oracle as orc
 
 from gpu_util import dev, golden, np64, rel_err, to_gpu
@@ -94,6 +95,7 @@ def _attn_case(dtype, hq, hkv, lq, d, segs, causal, seed):
                                           None if b is None else b.float().to(dev())) for k, v, b in segments],
                           causal=causal)
     torch.cuda.synchronize()
+    assert L.lib().dcc_device_error_status(1) == 0, "a bounded device wait expired"
     grp = hq // hkv
     for h in range(hq):
         qh = qd[h].double().numpy()
@@ -106,6 +108,7 @@ def _attn_case(dtype, hq, hkv, lq, d, segs, causal, seed):
             parts.append(orc.attention_partial(qh, kk, vv, bias=bb, positions=pos))
         want_o, want_l = orc.merge_lse([p[0] for p in parts], [p[1] for p in parts])
         tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+        assert np.isfinite(np64(o[h])).all()
         assert rel_err(np64(o[h]), want_o) < tol, h
         assert rel_err(np64(lse[h]), want_l) < (1e-2 if dtype == torch.bfloat16 else 1e-5)
 
@@ -122,3 +125,13 @@ def test_attention_biased_segments(dtype):
 
 def test_attention_small_head_dim_f32():
     _attn_case(torch.float32, 4, 2, 50, 32, [(50, False), (17, True)], True, 3)
+
+
+@pytest.mark.parametrize("hq,hkv,lq,segs,causal", [
+    (8, 2, 1000, [(1000, False)], True),                       # ragged causal, 8 tiles
+    (8, 2, 256, [(300, True), (128, True), (5, True)], False),  # three biased segments, ragged
+    (4, 1, 130, [(130, False), (64, True)], True),              # causal + compact in one launch
+    (2, 1, 64, [(1, True), (40, True)], False),                 # a one-key segment
+])
+def test_attention_tc05_shapes_bf16(hq, hkv, lq, segs, causal):
+    _attn_case(torch.bfloat16, hq, hkv, lq, 128, segs, causal, hq * 7 + lq)
