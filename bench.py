@@ -120,19 +120,31 @@ def dist_env():
 # ---------------------------------------------------------------------------
 # reference arm / CPU baseline: the FP64 oracle on a bounded sample
 # ---------------------------------------------------------------------------
-def cpu_sample(seconds_budget: float = 20.0):
+_CPU_INPUTS = None
+
+
+def _cpu_inputs():
+    """Block 0 (source) and the destination window of block 1, drawn once."""
+    global _CPU_INPUTS
+    if _CPU_INPUTS is None:
+        import numpy as np
+        from dcc_kv_b200.workloads import gqa_block
+        q, k, v = gqa_block(HQ, HKV, BLOCK_LEN, D, seed=1000, device="cpu")
+        q1, _, _ = gqa_block(HQ, HKV, BLOCK_LEN, D, seed=1001, device="cpu")
+        dq = np.concatenate([q1[j, :WINDOW].double().numpy() for j in range(4)])
+        _CPU_INPUTS = (q, k[0].double().numpy(), v[0].double().numpy(), dq)
+    return _CPU_INPUTS
+
+
+def cpu_sample():
     """Time the oracle on (a) one full-size edge build for one KV head and
     (b) attention of sampled query rows against full-size blocks, then
     extrapolate to the layer: 28 edges x 8 KV heads of builds and every
     (query row, visible key) pair of the local and compact attention."""
     import numpy as np
     from oracle import dcc_kv_oracle as orc
-    from dcc_kv_b200.workloads import gqa_block
 
-    q, k, v = gqa_block(HQ, HKV, BLOCK_LEN, D, seed=1000, device="cpu")
-    q1, _, _ = gqa_block(HQ, HKV, BLOCK_LEN, D, seed=1001, device="cpu")
-    k64, v64 = k[0].double().numpy(), v[0].double().numpy()
-    dq = np.concatenate([q1[j, :WINDOW].double().numpy() for j in range(4)])
+    q, k64, v64, dq = _cpu_inputs()
     t0 = time.perf_counter()
     qh, _ = orc.select_representative_queries(dq, M_REPR, DP)
     t_pool = time.perf_counter() - t0
@@ -184,45 +196,76 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+def _setup_dist():
+    import datetime
+    import torch.distributed as dist
+    ws, rank, local = dist_env()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    if ws > 1 and not dist.is_initialized():
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    return ws, rank, dev
+
+
+def _max_over_ranks(x: float, ws: int) -> float:
+    if ws == 1:
+        return x
+    import torch.distributed as dist
+    t = torch.tensor([x], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _barrier(ws: int) -> None:
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    torch.cuda.synchronize()
+
+
 def run_gpu(args):
     import dcc_kv_b200 as dk
-    from dcc_kv_b200.workloads import layer_inputs
+    from dcc_kv_b200.workloads import gqa_block, layer_inputs
 
-    ws, rank, local = dist_env()
-    if ws > 1:
-        from dcc_kv_b200.dist_layer import run_distributed_bench
-        return run_distributed_bench(args)
-    dev = torch.device("cuda", 0)
-    torch.cuda.set_device(dev)
-    q, k, v = layer_inputs(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, device="cuda")
-    layer = dk.DccKvSyncLayer(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, device=dev)
+    ws, rank, dev = _setup_dist()
+    if ws == 1:
+        q, k, v = layer_inputs(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, device="cuda")
+        layer = dk.DccKvSyncLayer(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, device=dev)
+        parallelism = "single GPU, 8 logical blocks"
+    else:
+        from dcc_kv_b200.dist_layer import DistributedDccKvLayer
+        blocks = [b for b in range(N_BLOCKS) if b % ws == rank]
+        parts = [gqa_block(HQ, HKV, BLOCK_LEN, D, 1000 + b, device="cuda") for b in blocks]
+        q, k, v = (torch.stack([p_[i] for p_ in parts]) for i in range(3))
+        layer = DistributedDccKvLayer(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, device=dev)
+        parallelism = f"context parallel over {ws} GPUs (block b on rank b % {ws}), NCCL all-to-allv of compacts"
     stream = torch.cuda.current_stream(dev)
-    for _ in range(max(args.warmup, 3)):
+    warmup = max(args.warmup, 3)
+    for _ in range(warmup):
         layer(q, k, v)
-    torch.cuda.synchronize()
-    # device-timed region: whole steps, plus the local-attention launch alone
+    _barrier(ws)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     attn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
                for _ in range(args.steps)]
     layer.timing_events = attn_ev
-    with ClockSampler(torch.cuda.current_device()) as clk:
-        torch.cuda.synchronize()
+    with ClockSampler(dev.index) as clk:
+        _barrier(ws)
         for i in range(args.steps):
             ev[i][0].record(stream)
             layer.timing_index = i
             layer(q, k, v)
             ev[i][1].record(stream)
-        torch.cuda.synchronize()
+        _barrier(ws)
     layer.timing_events = None
-    step_ms = [a.elapsed_time(b) for a, b in ev]
-    attn_ms = [a.elapsed_time(b) for a, b in attn_ev]
-    ms = sum(step_ms) / len(step_ms)
+    ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps, ws)
+    a_ms = sum(a.elapsed_time(b) for a, b in attn_ev) / args.steps
     clocks = clk.summary()
-    # end to end through the public API: pinned host inputs in, output back to host
+    # end to end through the public layer call: pinned host inputs in, output back to host
     hq_, hk_, hv_ = (t.cpu().pin_memory() for t in (q, k, v))
     out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
     dq, dk_, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     e2e_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    _barrier(ws)
     for i in range(args.steps + 1):
         if i > 0:
             e2e_ev[i - 1][0].record(stream)
@@ -233,34 +276,47 @@ def run_gpu(args):
         out_host.copy_(out, non_blocking=True)
         if i > 0:
             e2e_ev[i - 1][1].record(stream)
-    torch.cuda.synchronize()
-    e2e_ms = sum(a.elapsed_time(b) for a, b in e2e_ev) / args.steps
+    _barrier(ws)
+    e2e_ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in e2e_ev) / args.steps, ws)
+    h2d = _max_over_ranks(float(sum(t.numel() * t.element_size() for t in (q, k, v))), ws) * ws
+    d2h = float(out_host.numel() * out_host.element_size()) * ws
+    launches = layer.launches_per_forward() * args.steps
+    if rank != 0:
+        _teardown(ws)
+        return
     hbm, tf_burst, tf_sust, src = peaks()
-    local_flops, compact_flops = causal_attention_flops()
-    a_ms = sum(attn_ms) / len(attn_ms)
+    n_local = q.shape[0]
+    local_flops = n_local * HQ * (BLOCK_LEN * (BLOCK_LEN + 1) // 2) * 4 * D
     achieved = local_flops / (a_ms * 1e-3) / 1e12
     line = {
-        "metric": METRIC, "value": TOKENS / (ms * 1e-3), "unit": "tokens/s", "n_gpus": 1, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "metric": METRIC, "value": TOKENS / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws, "steps": args.steps,
+        "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
         "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1), 4 outlier channels x8 per KV head)",
-        "config": dict(WORKLOAD, parallelism="single GPU, 8 logical blocks"),
-        "e2e": {"value": TOKENS / (e2e_ms * 1e-3), "unit": "tokens/s",
-                "h2d_bytes_per_step": sum(t.numel() * t.element_size() for t in (q, k, v)),
-                "d2h_bytes_per_step": out_host.numel() * out_host.element_size()},
-        "gpu_launches": layer.launches_per_forward() * args.steps,
-        "roofline": {"kernel": "local causal attention (all 8 blocks, one launch)", "bound": "tensor",
-                     "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s", "frac": achieved / tf_sust,
-                     "peak_source": f"{src} bf16 sustained", "traffic": None,
+        "config": dict(WORKLOAD, parallelism=parallelism),
+        "e2e": {"value": TOKENS / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": int(h2d),
+                "d2h_bytes_per_step": int(d2h)},
+        "gpu_launches": launches,
+        "roofline": {"kernel": f"local causal attention ({n_local} block(s) per GPU, one launch, rank 0)",
+                     "bound": "tensor", "achieved": achieved, "peak": tf_sust, "unit": "TFLOP/s",
+                     "frac": achieved / tf_sust, "peak_source": f"{src} bf16 sustained", "traffic": None,
                      "algorithmic_flops": local_flops, "ms_per_launch": a_ms},
         "clocks": clocks,
     }
-    if args.cpu_baseline:
+    if args.cpu_baseline and ws == 1:
         cores = os.cpu_count() or 1
         torch.set_num_threads(cores)
         t, sample = cpu_sample()
         line["cpu_baseline"] = {"value": TOKENS / t, "unit": "tokens/s", "cores": cores, "kind": "port",
                                 "sample": sample}
     print(json.dumps(line), flush=True)
+    _teardown(ws)
+
+
+def _teardown(ws: int) -> None:
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def main():

@@ -19,7 +19,7 @@ int launch_attn_simt(const AttnBatch& b, const AttnParams& prm, int64_t max_lq, 
 int launch_attn_mma_bf16(const AttnBatch& b, const AttnParams& prm, int64_t max_lq, cudaStream_t st);
 
 // tcgen05 path: bf16, head_dim 128, an even number of query heads per KV head,
-// at most 4 KV segments per problem.
+// at most 8 KV segments per problem.
 bool attn_tc05_supported(const dcc_attn_problem& p, const AttnParams& prm);
 int launch_attn_tc05(const dcc_attn_problem* probs, int n, const AttnParams& prm, cudaStream_t st);
 

@@ -33,8 +33,8 @@ namespace dcc {
 
 using namespace tc05;
 
-constexpr int kTcMaxSeg = 4;
-constexpr int kTcCap = 12;
+constexpr int kTcMaxSeg = 8;
+constexpr int kTcCap = 8;
 
 struct Tc05Seg {
   CUtensorMap k;  // {128, len, n_kv_heads}, box {64, 128, 1}, 128B swizzle

@@ -1,0 +1,233 @@
+"""The DCC-KV sync layer sharded by sequence block over one process per GPU.
+
+Logical block b lives on rank b % G (round-robin, so the causal load --
+more compact blocks for later blocks, more builds for earlier ones --
+balances across ranks).  One forward on every rank:
+
+  0. pooling: representative queries of the local destination blocks
+     (FP64 FPS), then ``all_gather`` of the [n_local, H_kv, M, d] tensors
+     (the only collective before the exchange; ~128 KB per rank);
+  1. builds: every local source s builds C_{s->r} for every r > s, written
+     straight into the wire layout (var_len_msg.EdgeLayout) of a
+     per-destination-rank send buffer (edges between co-resident blocks go
+     to a local buffer and never touch NCCL);
+  2. exchange: one NCCL all-to-allv of the byte buffers on a side stream,
+     sizes known from the shared budget table (no size round trip);
+  3. local causal attention on the main stream, overlapped with (2);
+  4. compact attention with logit bias, one KV segment per source edge,
+     read in place from the receive / local buffers;
+  5. online-softmax merge into the local output.
+
+``DistPlan`` is the pure host-side routing (offsets and split sizes),
+identical on every rank and testable without a GPU.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, List, Tuple
+
+import torch
+import torch.distributed as dist
+
+from . import _lib as L
+from .attention import attn_problem, kv_segment, run_attention
+from .compact_kv import build_problem, run_build_problems
+from .layer import Budgets, budget_table
+from .online_softmax import merge_lse
+from .representative_query import query_set, select_query_sets
+from .var_len_msg import EdgeLayout
+
+
+class DistPlan:
+    """Routing of every compact-KV edge (s -> r, s < r) for G ranks."""
+
+    def __init__(self, n_blocks: int, world: int, block_len: int, n_kv_heads: int, head_dim: int,
+                 budgets: Budgets, elem_bytes: int = 2):
+        if n_blocks % world:
+            raise ValueError(f"{n_blocks} blocks do not split evenly over {world} ranks")
+        self.nb, self.world, self.L = n_blocks, world, block_len
+        self.n_local = n_blocks // world
+        self.budgets = budget_table(n_blocks, budgets)
+        self.layout = {e: EdgeLayout(n_kv_heads, min(b, block_len), head_dim, elem_bytes)
+                       for e, b in self.budgets.items()}
+        # bytes from rank i to rank j: edges (s on i, r on j), ordered by (r, s)
+        self.edges_ij = {(i, j): sorted(((s, r) for (s, r) in self.budgets if self.owner(s) == i
+                                         and self.owner(r) == j), key=lambda e: (e[1], e[0]))
+                         for i in range(world) for j in range(world)}
+        self.bytes_ij = {ij: sum(self.layout[e].nbytes for e in es) for ij, es in self.edges_ij.items()}
+
+    def owner(self, b: int) -> int:
+        return b % self.world
+
+    def local_index(self, b: int) -> int:
+        return b // self.world
+
+    def local_blocks(self, rank: int) -> List[int]:
+        return [b for b in range(self.nb) if self.owner(b) == rank]
+
+    def send_splits(self, rank: int) -> List[int]:
+        return [0 if j == rank else self.bytes_ij[(rank, j)] for j in range(self.world)]
+
+    def recv_splits(self, rank: int) -> List[int]:
+        return [0 if i == rank else self.bytes_ij[(i, rank)] for i in range(self.world)]
+
+    def send_offsets(self, rank: int) -> Dict[Tuple[int, int], Tuple[str, int]]:
+        """Where rank's builds write each outgoing edge: ("send"|"local", byte offset)."""
+        out, off = {}, 0
+        for j in range(self.world):
+            if j == rank:
+                continue
+            for e in self.edges_ij[(rank, j)]:
+                out[e] = ("send", off)
+                off += self.layout[e].nbytes
+        off = 0
+        for e in self.edges_ij[(rank, rank)]:
+            out[e] = ("local", off)
+            off += self.layout[e].nbytes
+        return out
+
+    def recv_offsets(self, rank: int) -> Dict[Tuple[int, int], Tuple[str, int]]:
+        """Where each incoming edge (s -> r, r on rank) sits: ("recv"|"local", byte offset)."""
+        out, off = {}, 0
+        for i in range(self.world):
+            if i == rank:
+                continue
+            for e in self.edges_ij[(i, rank)]:
+                out[e] = ("recv", off)
+                off += self.layout[e].nbytes
+        for e, loc in self.send_offsets(rank).items():
+            if loc[0] == "local":
+                out[e] = loc
+        return out
+
+
+class DistributedDccKvLayer:
+    """One process per GPU; block-major local inputs
+    q [n_local, H_q, L, d], k / v [n_local, H_kv, L, d] for the blocks
+    rank, rank + G, rank + 2G, ... of the context."""
+
+    def __init__(self, n_blocks: int, block_len: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
+                 budgets: Budgets, window: int, num_representative_queries: int = 64, projection_dim: int = 32,
+                 lambda_beta: float = 1e-3, lambda_value: float = 1e-3, seed: int = 42,
+                 dtype: torch.dtype = torch.bfloat16, device=None, group=None):
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.nb, self.L, self.hq, self.hkv, self.d = n_blocks, block_len, n_q_heads, n_kv_heads, head_dim
+        self.qgroup = n_q_heads // n_kv_heads
+        self.window = min(window, block_len)
+        self.M = num_representative_queries
+        self.m_eff = min(self.M, self.qgroup * self.window)
+        self.dp, self.lb, self.lv, self.seed = projection_dim, lambda_beta, lambda_value, seed
+        self.dtype = dtype
+        self.code = L.dtype_code(torch.empty(0, dtype=dtype))
+        self.plan = DistPlan(n_blocks, self.world, block_len, n_kv_heads, head_dim, budgets,
+                             torch.empty(0, dtype=dtype).element_size())
+        self.n_local = self.plan.n_local
+        self.local_blocks = self.plan.local_blocks(self.rank)
+        dev = self.device
+        self.repr_local = torch.zeros(self.n_local, n_kv_heads, self.m_eff, head_dim, dtype=dtype, device=dev)
+        self.repr_idx = torch.empty(self.n_local, n_kv_heads, self.m_eff, dtype=torch.int64, device=dev)
+        self.repr_all = torch.empty(self.world, self.n_local, n_kv_heads, self.m_eff, head_dim, dtype=dtype,
+                                    device=dev)
+        send_splits = self.plan.send_splits(self.rank)
+        recv_splits = self.plan.recv_splits(self.rank)
+        self.send_splits, self.recv_splits = send_splits, recv_splits
+        local_bytes = self.plan.bytes_ij[(self.rank, self.rank)]
+        self.send_buf = torch.empty(max(sum(send_splits), 256), dtype=torch.uint8, device=dev)
+        self.recv_buf = torch.empty(max(sum(recv_splits), 256), dtype=torch.uint8, device=dev)
+        self.local_buf = torch.empty(max(local_bytes, 256), dtype=torch.uint8, device=dev)
+        self.bufs = {"send": self.send_buf, "recv": self.recv_buf, "local": self.local_buf}
+        # per-edge selected indices stay on the source rank
+        self.sel_idx = {e: torch.empty(n_kv_heads, self.plan.layout[e].rows, dtype=torch.int64, device=dev)
+                        for e, loc in self.plan.send_offsets(self.rank).items()}
+        self.o_loc = torch.empty(self.n_local, n_q_heads, block_len, head_dim, dtype=dtype, device=dev)
+        self.lse_loc = torch.empty(self.n_local, n_q_heads, block_len, dtype=torch.float32, device=dev)
+        self.o_c = torch.empty_like(self.o_loc)
+        self.lse_c = torch.empty_like(self.lse_loc)
+        self.comm_stream = torch.cuda.Stream(device=dev)
+        self._bound = None
+        self.timing_events = None
+        self.timing_index = 0
+
+    def _bind(self, q, k, v):
+        key = (q.data_ptr(), k.data_ptr(), v.data_ptr())
+        if self._bound == key:
+            return
+        g = self.qgroup
+        self.sets = [query_set(q[li, h * g], self.repr_local[li, h], self.repr_idx[li, h], n_seg=g,
+                               seg_rows=self.window, seg_stride=q.stride(1), row_stride=q.stride(2))
+                     for li, b in enumerate(self.local_blocks) if b > 0 for h in range(self.hkv)]
+        send_off = self.plan.send_offsets(self.rank)
+        self.build = []
+        for (s, r), (buf, off) in sorted(send_off.items()):
+            lay = self.plan.layout[(s, r)]
+            ko, vo, bo = lay.views(self.bufs[buf], off, self.dtype)
+            rep = self.repr_all[self.plan.owner(r), self.plan.local_index(r)]
+            ls = self.plan.local_index(s)
+            for h in range(self.hkv):
+                self.build.append(build_problem(k[ls, h], v[ls, h], rep[h], self.plan.budgets[(s, r)], ko[h], vo[h],
+                                                bo[h], self.sel_idx[(s, r)][h], num_repr=self.m_eff))
+        self._ws = None
+        if self.build:
+            arr = (L.dcc_build_problem * len(self.build))(*self.build)
+            need = L.lib().dcc_build_compact_kv_workspace_bytes(arr, len(self.build), self.d, self.d, self.code)
+            self._ws = L.workspace(need, self.device)
+        self.local_problems = [attn_problem(q[li], self.o_loc[li], self.lse_loc[li], [kv_segment(k[li], v[li])],
+                                            causal=True) for li in range(self.n_local)]
+        recv_off = self.plan.recv_offsets(self.rank)
+        self.compact_problems, self.merge_rows = [], []
+        for li, r in enumerate(self.local_blocks):
+            segs = []
+            for s in range(r):
+                buf, off = recv_off[(s, r)]
+                ko, vo, bo = self.plan.layout[(s, r)].views(self.bufs[buf], off, self.dtype)
+                segs.append(kv_segment(ko, vo, bo))
+            if segs:
+                self.compact_problems.append(attn_problem(q[li], self.o_c[li], self.lse_c[li], segs))
+                self.merge_rows.append(li)
+        self._bound = key
+
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        exp_q = (self.n_local, self.hq, self.L, self.d)
+        exp_kv = (self.n_local, self.hkv, self.L, self.d)
+        if tuple(q.shape) != exp_q or tuple(k.shape) != exp_kv or tuple(v.shape) != exp_kv:
+            raise ValueError(f"expected local q {exp_q}, k/v {exp_kv}")
+        for t in (q, k, v):
+            if t.dtype != self.dtype or not t.is_contiguous() or t.device != self.device:
+                raise ValueError(f"inputs must be contiguous {self.dtype} on {self.device}")
+        self._bind(q, k, v)
+        dev = self.device
+        main = torch.cuda.current_stream(dev)
+        select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
+        dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.group)
+        run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
+        # exchange on the side stream, local attention meanwhile
+        self.comm_stream.wait_stream(main)
+        with torch.cuda.stream(self.comm_stream):
+            dist.all_to_all_single(self.recv_buf[: sum(self.recv_splits)] if sum(self.recv_splits) else self.recv_buf[:0],
+                                   self.send_buf[: sum(self.send_splits)] if sum(self.send_splits) else self.send_buf[:0],
+                                   output_split_sizes=self.recv_splits, input_split_sizes=self.send_splits,
+                                   group=self.group)
+        scale = 1.0 / math.sqrt(self.d)
+        ev = self.timing_events[self.timing_index] if self.timing_events else None
+        if ev is not None:
+            ev[0].record(main)
+        run_attention(self.local_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
+        if ev is not None:
+            ev[1].record(main)
+        main.wait_stream(self.comm_stream)
+        run_attention(self.compact_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
+        for li in self.merge_rows:
+            merge_lse([self.o_loc[li], self.o_c[li]], [self.lse_loc[li], self.lse_c[li]], out=self.o_loc[li],
+                      want_lse=False)
+        return self.o_loc
+
+    __call__ = forward
+
+    def launches_per_forward(self) -> int:
+        sets = len(self.sets)
+        pool = 0 if sets == 0 else 2 * -(-sets // 64)
+        return (pool + 4 * -(-len(self.build) // 96) + -(-len(self.local_problems) // 8)
+                + -(-len(self.compact_problems) // 8) + len(self.merge_rows))

@@ -159,11 +159,11 @@ class DccKvSyncLayer:
 
     def launches_per_forward(self) -> int:
         """Kernel launches one forward enqueues (batch caps of the C library:
-        64 query sets, 96 build edges, 24 attention problems per launch)."""
+        64 query sets, 96 build edges, 8 tcgen05 attention problems per launch)."""
         sets = len(self.sets)
         pool = 0 if sets == 0 else (2 if self.m_eff < self.group * self.window else 1) * -(-sets // 64)
         build = 4 * -(-len(self.build) // 96)
-        attn = -(-len(self.local_problems) // 24) + -(-len(self.compact_problems) // 24)
+        attn = -(-len(self.local_problems) // 8) + -(-len(self.compact_problems) // 8)
         return pool + build + attn + (1 if self.nb > 1 else 0)
 
     def compact(self, s: int, r: int, h: int):

@@ -1,0 +1,78 @@
+"""Worker functions for the multi-process (gloo, CPU) tests; a module of its
+own so spawned children can import them."""
+from __future__ import annotations
+
+import os
+import traceback
+
+import torch
+import torch.distributed as dist
+
+
+def _init(rank: int, world: int, port: int) -> None:
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+
+
+def _pattern(edge, nbytes: int) -> torch.Tensor:
+    s, r = edge
+    return ((torch.arange(nbytes, dtype=torch.int64) * 7 + 31 * s + 131 * r) % 251).to(torch.uint8)
+
+
+def exchange_worker(rank: int, world: int, port: int, n_blocks: int, budgets, errq) -> None:
+    """Fill the send/local buffers per DistPlan, exchange with the plan's
+    splits, check every incoming edge lands where recv_offsets says."""
+    try:
+        from dcc_kv_b200.dist_layer import DistPlan
+        _init(rank, world, port)
+        plan = DistPlan(n_blocks, world, 512, 2, 16, budgets)
+        send = torch.zeros(max(sum(plan.send_splits(rank)), 1), dtype=torch.uint8)
+        local = torch.zeros(max(plan.bytes_ij[(rank, rank)], 1), dtype=torch.uint8)
+        bufs = {"send": send, "local": local}
+        for e, (buf, off) in plan.send_offsets(rank).items():
+            n = plan.layout[e].nbytes
+            bufs[buf][off:off + n] = _pattern(e, n)
+        recv = torch.zeros(max(sum(plan.recv_splits(rank)), 1), dtype=torch.uint8)
+        ss, rs = plan.send_splits(rank), plan.recv_splits(rank)
+        dist.all_to_all_single(recv[:sum(rs)], send[:sum(ss)], output_split_sizes=rs, input_split_sizes=ss)
+        bufs["recv"] = recv
+        for e, (buf, off) in plan.recv_offsets(rank).items():
+            n = plan.layout[e].nbytes
+            assert plan.owner(e[1]) == rank
+            if not torch.equal(bufs[buf][off:off + n], _pattern(e, n)):
+                raise AssertionError(f"rank {rank}: edge {e} wrong at {buf}+{off}")
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put(traceback.format_exc())
+
+
+def comm_worker(rank: int, world: int, port: int, errq) -> None:
+    """DistributedComm.all_to_all_v contents over gloo (reference
+    tests/test_smoke.py:237-285 restated)."""
+    try:
+        from dcc_kv_b200.comm import DistributedComm, VarLenMessage
+        _init(rank, world, port)
+        comm = DistributedComm(backend="gloo")
+        comm.init(rank, world)
+        # rank i sends (i + 1) * (j + 1) rows of value 100 * i + j to rank j
+        msgs = [VarLenMessage(payload=torch.full(((rank + 1) * (j + 1), 3), float(100 * rank + j)))
+                for j in range(world)]
+        recv_sizes = [(i + 1) * (rank + 1) for i in range(world)]
+        for trust in (False, True):
+            out = comm.all_to_all_v(msgs, recv_sizes=recv_sizes, trust_recv_sizes=trust)
+            for i, m in enumerate(out):
+                assert m.metadata["src_rank"] == i
+                assert m.payload.shape == (recv_sizes[i], 3)
+                assert torch.all(m.payload == float(100 * i + rank))
+        t = torch.tensor([float(rank + 1)])
+        assert comm.all_reduce(t).item() == sum(range(1, world + 1))
+        g = comm.gather(torch.tensor([rank]), dst=0)
+        if rank == 0:
+            assert [x.item() for x in g] == list(range(world))
+        comm.barrier()
+        comm.cleanup()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put(traceback.format_exc())

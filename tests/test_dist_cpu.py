@@ -1,0 +1,155 @@
+"""Host logic of the sharded layer and the communication layer, on CPU:
+the routing plan (every edge sent once, received where the destination
+reads it), a real gloo all-to-allv of byte buffers laid out by the plan
+(world sizes 2 and 4), DistributedComm in mock and gloo modes, and the
+var-len codec (the reference's tests/test_var_len_msg.py and
+tests/test_smoke.py restated)."""
+from __future__ import annotations
+
+import multiprocessing as pymp
+import random
+
+import pytest
+import torch
+
+from dcc_kv_b200.comm import DistributedComm, VarLenMessage
+from dcc_kv_b200.dist_layer import DistPlan
+from dcc_kv_b200.var_len_msg import (EdgeLayout, mock_all_to_allv, pack_var_len_messages,
+                                     unpack_var_len_messages)
+
+import dist_workers
+
+
+def _spawn(target, world, *args):
+    ctx = pymp.get_context("spawn")
+    errq = ctx.Queue()
+    port = random.randint(20000, 40000)
+    procs = [ctx.Process(target=target, args=(r, world, port) + args + (errq,)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=120)
+    alive = [p for p in procs if p.is_alive()]
+    for p in alive:
+        p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not alive, "a rank did not finish"
+    assert not errors, "\n".join(errors)
+    assert all(p.exitcode == 0 for p in procs)
+
+
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_plan_routes_every_edge_once(world):
+    budgets = {(s, r): [256, 512, 1024, 2048][(s * 3 + r) % 4] for r in range(8) for s in range(r)}
+    plan = DistPlan(8, world, 16384, 8, 128, budgets)
+    sent, received = {}, {}
+    for rank in range(world):
+        for e, loc in plan.send_offsets(rank).items():
+            assert plan.owner(e[0]) == rank and e not in sent
+            sent[e] = (rank, loc)
+        for e, loc in plan.recv_offsets(rank).items():
+            assert plan.owner(e[1]) == rank and e not in received
+            received[e] = (rank, loc)
+        # byte ranges of one buffer never overlap
+        for offsets in (plan.send_offsets(rank), plan.recv_offsets(rank)):
+            spans = sorted((buf, off, off + plan.layout[e].nbytes) for e, (buf, off) in offsets.items())
+            for a, b in zip(spans, spans[1:]):
+                assert a[0] != b[0] or a[2] <= b[1]
+    assert set(sent) == set(received) == set(budgets)
+    for i in range(world):
+        for j in range(world):
+            assert plan.send_splits(i)[j] == plan.recv_splits(j)[i]
+    # every block sits on exactly one rank, round-robin
+    assert sorted(b for r in range(world) for b in plan.local_blocks(r)) == list(range(8))
+
+
+def test_plan_rejects_uneven_split():
+    with pytest.raises(ValueError):
+        DistPlan(8, 3, 128, 2, 16, 64)
+
+
+def test_edge_layout_alignment():
+    for rows in (1, 45, 64, 1024):
+        lay = EdgeLayout(3, rows, 128, 2)
+        assert lay.nbytes % 256 == 0
+        assert lay.values_off % 16 == 0 and lay.bias_off % 16 == 0
+        buf = torch.zeros(lay.nbytes * 2, dtype=torch.uint8)
+        k, v, b = lay.views(buf, lay.nbytes, torch.bfloat16)
+        assert k.shape == (3, rows, 128) and b.shape == (3, rows)
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_gloo_exchange_by_plan(world):
+    budgets = {(s, r): [17, 64, 100][(s + r) % 3] for r in range(8) for s in range(r)}
+    _spawn(dist_workers.exchange_worker, world, 8, budgets)
+
+
+def test_gloo_distributed_comm_all_to_all_v():
+    _spawn(dist_workers.comm_worker, 2)
+
+
+# ---- DistributedComm, mock mode and errors (reference tests/test_smoke.py:67-157, :306-340)
+def test_comm_mock_lifecycle_and_shapes():
+    comm = DistributedComm(backend="gloo", mock=True)
+    assert not comm.initialized
+    comm.init(rank=0, world_size=2)
+    assert comm.initialized and comm.rank == 0 and comm.world_size == 2
+    recv = comm.all_to_all_single(torch.tensor([1.0, 2.0, 3.0, 4.0]), send_counts=[2, 2], recv_counts=[2, 2])
+    assert recv.shape == (4,) and torch.all(recv == 0)
+    msgs = [VarLenMessage(payload=torch.tensor([1.0, 2.0])), VarLenMessage(payload=torch.tensor([3.0, 4.0, 5.0]))]
+    res = comm.all_to_all_v(msgs, send_sizes=[2, 3], recv_sizes=[3, 2])
+    assert [r.payload.shape for r in res] == [(3,), (2,)]
+    assert res[0].metadata["src_rank"] == 0 and res[1].metadata["src_rank"] == 1
+    t = torch.tensor([1.0])
+    assert torch.equal(comm.all_reduce(t), t)
+    comm.cleanup()
+    assert not comm.initialized
+
+
+def test_comm_errors():
+    with pytest.raises(ValueError):
+        DistributedComm(backend="tcp")
+    comm = DistributedComm(mock=True)
+    with pytest.raises(RuntimeError):
+        comm.all_to_all_v([], recv_sizes=[])
+    comm.init(0, 2)
+    with pytest.raises(ValueError):
+        comm.all_to_all_v([VarLenMessage(torch.zeros(1))], recv_sizes=[1, 1])
+    with pytest.raises(ValueError):
+        comm.all_to_all_v([VarLenMessage(torch.zeros(1))] * 2, recv_sizes=None)
+    with pytest.raises(ValueError):
+        comm.all_to_all_v([VarLenMessage(torch.zeros(1))] * 2, send_sizes=[2, 1], recv_sizes=[1, 1])
+    with pytest.raises(ValueError):
+        comm.all_to_all_single(torch.zeros(5), send_counts=[2, 2])
+    real = DistributedComm(backend="gloo", mock=False)
+    with pytest.raises(RuntimeError):
+        real.init(0, 2)  # torch.distributed not initialised
+
+
+# ---- var-len codec (reference tests/test_var_len_msg.py:23-97)
+def test_var_len_round_trips():
+    msgs = [torch.tensor([1.0, 2.0]), torch.tensor([3.0]), torch.tensor([4.0, 5.0, 6.0])]
+    packed, offsets = pack_var_len_messages(msgs, [2, 1, 3])
+    assert packed.shape == (6,) and offsets == [0, 2, 3, 6]
+    for a, b in zip(msgs, unpack_var_len_messages(packed, [2, 1, 3])):
+        assert torch.equal(a, b)
+    msgs2 = [torch.randn(2, 64), torch.randn(3, 64), torch.randn(5, 64)]
+    packed2, offsets2 = pack_var_len_messages(msgs2, [2, 3, 5])
+    assert packed2.shape == (10, 64) and offsets2 == [0, 2, 5, 10]
+    with pytest.raises(AssertionError):
+        pack_var_len_messages([torch.tensor([1.0, 2.0]), torch.tensor([3.0])], sizes=[2, 3])
+
+
+def test_mock_all_to_allv_two_ranks():
+    m00, m01 = torch.tensor([1.0, 2.0]), torch.tensor([10.0, 11.0, 12.0])
+    m10, m11 = torch.tensor([100.0, 101.0, 102.0]), torch.tensor([200.0, 201.0])
+    p0, _ = pack_var_len_messages([m00, m01], [2, 3])
+    p1, _ = pack_var_len_messages([m10, m11], [3, 2])
+    r0 = mock_all_to_allv(0, 2, [m00, m01], [2, 3], {1: (p1, [3, 2])})
+    r1 = mock_all_to_allv(1, 2, [m10, m11], [3, 2], {0: (p0, [2, 3])})
+    assert torch.equal(r0[0], m00) and torch.equal(r0[1], m10)
+    assert torch.equal(r1[0], m01) and torch.equal(r1[1], m11)
+    with pytest.raises(ValueError):
+        mock_all_to_allv(0, 2, [m00, m01], [2, 3], {})
