@@ -104,6 +104,7 @@ SIGNATURES = {
     "dcc_ridge_regression_value": (_I, [_P, _P, _I64, _I64, _I64, _D, _I, _P, _P, _SZ, _P]),
     "dcc_attention_fwd": (_I, [_P, _I, _I, _I, _I, _D, _I, _P]),
     "dcc_device_error_status": (_I, [_I]),
+    "dcc_build_error_status": (_I, [_I]),
     "dcc_online_softmax_from_attention": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P]),
     "dcc_merge_softmax_states": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _P, _P, _P, _P]),
     "dcc_merge_lse": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _P, _P]),

@@ -10,6 +10,8 @@
 // so the three softmaxes of the reference over the same logits become two
 // streaming reads of K and one of V.  Chunk partials are combined in a fixed
 // order (deterministic).
+#include <type_traits>
+
 #include "build_common.cuh"
 
 namespace dcc {
@@ -201,9 +203,16 @@ __global__ void __launch_bounds__(256) score_probs_kernel(const __grid_constant_
   }
 }
 
+bool scoring_tc05_supported(const BuildBatch<float>& b, const BuildParams& prm);
+int launch_scoring_tc05(const BuildBatch<float>& b, const BuildParams& prm, int max_chunks, cudaStream_t st);
+
 template <typename TIn, typename Acc>
 int launch_scoring(const BuildBatch<Acc>& b, const BuildParams& prm, int max_chunks,
                    cudaStream_t st) {
+  if constexpr (std::is_same<TIn, __nv_bfloat16>::value) {
+    // bf16, d = dv = 128, M <= 64: the tensor-core passes (scoring_tc05.cu)
+    if (scoring_tc05_supported(b, prm)) return launch_scoring_tc05(b, prm, max_chunks, st);
+  }
   const int ld = prm.d + 1, ldv = prm.dv + 1;
   const size_t smem1 = (size_t)(kMaxRepr + kScoreTile) * ld * sizeof(Acc);
   const size_t smem2 = ((size_t)(kMaxRepr + kScoreTile) * ld + (size_t)kScoreTile * ldv +

@@ -231,6 +231,8 @@ int dcc_attention_fwd(const dcc_attn_problem* problems, int n_problems, int n_q_
  * wait of the tcgen05 attention kernel expired since the last clear
  * (DCC_ERR_TIMEOUT), clearing the flag when `clear` is non-zero. */
 int dcc_device_error_status(int clear);
+/* The same for the tcgen05 scoring passes of the compact-KV build. */
+int dcc_build_error_status(int clear);
 
 /* ---- online softmax ------------------------------------------------------
  * online_softmax_from_attention (online_softmax.py:52-89), batched: logits

@@ -40,3 +40,10 @@ def build_inputs(f, name):
         Q = torch.randn(512, 128, generator=g, dtype=torch.float64).numpy()
         return K, V, Q
     return f["K"].astype(np.float64), f["V"].astype(np.float64), f["Q"].astype(np.float64)
+
+
+def assert_no_device_timeouts():
+    """No bounded device-side wait (tcgen05 attention, tcgen05 scoring) expired."""
+    from dcc_kv_b200 import _lib as L
+    assert L.lib().dcc_device_error_status(1) == 0, "attention: a bounded device wait expired"
+    assert L.lib().dcc_build_error_status(1) == 0, "scoring: a bounded device wait expired"

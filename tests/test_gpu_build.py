@@ -20,7 +20,7 @@ import dcc_kv_b200 as dk
 from oracle import dcc_kv_oracle as orc
 
 from conftest import GOLDEN
-from gpu_util import build_inputs, dev, golden, np64, rel_err, to_gpu
+from gpu_util import assert_no_device_timeouts, build_inputs, dev, golden, np64, rel_err, to_gpu
 
 pytestmark = pytest.mark.gpu
 
@@ -120,6 +120,7 @@ def test_gqa_batched_build_full_size_bf16():
         repr_q.append(rep)
     comps = dk.build_compact_kv_batched(k.to(dev()), v.to(dev()), torch.stack(repr_q), 512)
     torch.cuda.synchronize()
+    assert_no_device_timeouts()
     for h in (0, 5):
         dq = np.concatenate([q[4 * h + j].double().numpy() for j in range(4)])
         ref = orc.build_compact_kv(k[h].double().numpy(), v[h].double().numpy(), dq, 512)

@@ -18,7 +18,7 @@ import torch
 import dcc_kv_b200 as dk
 from oracle import dcc_kv_oracle as orc
 
-from gpu_util import dev, golden, np64, rel_err, to_gpu
+from gpu_util import assert_no_device_timeouts, dev, golden, np64, rel_err, to_gpu
 
 pytestmark = pytest.mark.gpu
 
@@ -75,6 +75,7 @@ def test_layer_bf16_small():
     layer = dk.DccKvSyncLayer(nb, L, hq, hkv, d, budgets, window=128)
     out = layer(q.to(dev()), k.to(dev()), v.to(dev()))
     torch.cuda.synchronize()
+    assert_no_device_timeouts()
     ref, _ = _oracle_layer(q, k, v, budgets, 128, 64, 32)
     for r in range(nb):
         assert rel_err(np64(out[r]), ref[r]) < 2e-2, r
@@ -88,6 +89,7 @@ def test_layer_full_128k_bf16_sampled():
     layer = dk.DccKvSyncLayer(nb, L, hq, hkv, d, 1024, window=2048)
     out = layer(q.to(dev()), k.to(dev()), v.to(dev()))
     torch.cuda.synchronize()
+    assert_no_device_timeouts()
     rows = {b: np.array([0, 1, 777, 8191, 16383]) for b in range(nb)}
     # oracle over three blocks (building every edge into them), sampled rows
     sub = [0, 1, 2]
