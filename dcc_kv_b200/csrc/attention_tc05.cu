@@ -114,6 +114,13 @@ __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
 }
 
+// 2^x on the SFU (ex2.approx.ftz: ~2 ulp, 2^-inf = 0).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
@@ -157,7 +164,7 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
     for (int i = 0; i < 4; ++i) {
       const int c = lane * 4 + i;
       const int64_t key = t.t0 + c;
-      sm.bias[st][c] = (bg && key < t.kend) ? __ldg(bg + key) : 0.f;
+      sm.bias[st][c] = (bg && key < t.kend) ? __ldg(bg + key) * 1.4426950408889634f : 0.f;  // log2 units
     }
     mbar_arrive(&sm.bar_bias[st]);
     issued = j + 1;
@@ -174,50 +181,67 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
 }
 
 // ---- MMA issuer (warp 9) -----------------------------------------------------------
+// Issue order per tile j:  PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)  (S_A(0), S_B(0) first),
+// so head A's next scores are ready while head B's softmax still runs.  S(j+1)
+// overwrites P(j) in TMEM only after PV(j), issued earlier from this thread.
 __device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int lane) {
   const uint32_t id_s = idesc_bf16_f32(128, 128, 0, 0);
   const uint32_t id_pv = idesc_bf16_f32(128, 128, 0, 1);
   bool ok = warp_wait(&sm.bar_q, 0);
   int done = 0;
+  auto issue_s = [&](int h, int st) {
+    if (lane == 0) {
+      const uint32_t s_col = h ? kColSB : kColSA;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) umma_ss(tm + s_col, kdesc(sm.q[h], kk), kdesc(sm.k[st], kk), id_s, kk > 0);
+      umma_commit(&sm.bar_s[h]);
+    }
+    __syncwarp();
+  };
+  auto issue_pv = [&](int h, int st, int j) {
+    if (lane == 0) {
+      const uint32_t o_col = h ? kColOB : kColOA, p_col = h ? kColSB : kColSA;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk)
+        umma_ts(tm + o_col, tm + p_col + kk * 8, vdesc(sm.v[st], kk), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+      umma_commit(&sm.bar_o[h]);
+    }
+    __syncwarp();
+  };
+  if (ok && n_tiles > 0) {
+    ok = warp_wait(&sm.bar_k[0], 0);
+    if (ok) {
+      tc_fence_after();
+      issue_s(0, 0);
+      issue_s(1, 0);
+    }
+  }
   for (int j = 0; j < n_tiles && ok; ++j) {
-    const int st = j & 1;
-    const uint32_t ph = (j >> 1) & 1;
-    if (!warp_wait(&sm.bar_k[st], ph)) {
+    const int st = j & 1, st1 = (j + 1) & 1;
+    const bool more = j + 1 < n_tiles;
+    if (!warp_wait(&sm.bar_v[st], (j >> 1) & 1) || !warp_wait(&sm.bar_p[0], j & 1)) {
       ok = false;
       break;
     }
     tc_fence_after();
-    if (lane == 0) {
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) umma_ss(tm + kColSA, kdesc(sm.q[0], kk), kdesc(sm.k[st], kk), id_s, kk > 0);
-      umma_commit(&sm.bar_s[0]);
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) umma_ss(tm + kColSB, kdesc(sm.q[1], kk), kdesc(sm.k[st], kk), id_s, kk > 0);
-      umma_commit(&sm.bar_s[1]);
-    }
-    __syncwarp();
-    if (!warp_wait(&sm.bar_v[st], ph)) {
-      ok = false;
-      break;
-    }
-    for (int h = 0; h < 2 && ok; ++h) {
-      if (!warp_wait(&sm.bar_p[h], j & 1)) {
+    issue_pv(0, st, j);
+    if (more) {
+      if (!warp_wait(&sm.bar_k[st1], ((j + 1) >> 1) & 1)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      if (lane == 0) {
-        const uint32_t o_col = h ? kColOB : kColOA, p_col = h ? kColSB : kColSA;
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          umma_ts(tm + o_col, tm + p_col + kk * 8, vdesc(sm.v[st], kk), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(&sm.bar_o[h]);
-      }
-      __syncwarp();
+      issue_s(0, st1);
     }
-    if (!ok) break;
+    if (!warp_wait(&sm.bar_p[1], j & 1)) {
+      ok = false;
+      break;
+    }
+    tc_fence_after();
+    issue_pv(1, st, j);
     if (lane == 0) umma_commit(&sm.bar_empty[st]);
     __syncwarp();
+    if (more) issue_s(1, st1);
     done = j + 1;
   }
   if (!ok) atomicOr(&g_attn_error, 2u);
@@ -234,7 +258,6 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
   const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
   const uint32_t s_col = role ? kColSB : kColSA, o_col = role ? kColOB : kColOA;
   const int64_t q_row = q0 + row;
-  const float kLog2e = 1.4426950408889634f;
   float m_use = -INFINITY, l = 0.f;
   bool ok = true;
   for (int j = 0; j < n_tiles; ++j) {
@@ -254,16 +277,24 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
       ok = false;
       break;
     }
-    float mt = -INFINITY;
+    // visible keys of this row in the tile: [t0, t0 + nvis)
     const int64_t lim = causal ? q_row + p.causal_offset : t.kend - 1;  // last visible key
     const int64_t lim2 = lim < t.kend - 1 ? lim : t.kend - 1;
     const int nvis = (int)(lim2 - t.t0 + 1 < 0 ? 0 : (lim2 - t.t0 + 1 > 128 ? 128 : lim2 - t.t0 + 1));
+    const bool plain = __all_sync(0xffffffffu, nvis == 128) && !p.seg[t.seg].bias;
+    float mt = -INFINITY;
+    if (plain) {
+      // whole tile visible, no bias: max of the raw scores, scaled once
 #pragma unroll
-    for (int c = 0; c < 128; ++c) {
-      float x = fmaf(s[c], b.scale_log2, sm.bias[st][c] * kLog2e);
-      x = c < nvis ? x : -INFINITY;
-      s[c] = x;
-      mt = fmaxf(mt, x);
+      for (int c = 0; c < 128; ++c) mt = fmaxf(mt, s[c]);
+      mt *= b.scale_log2;
+    } else {
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float x = c < nvis ? fmaf(s[c], b.scale_log2, sm.bias[st][c]) : -INFINITY;
+        s[c] = x;
+        mt = fmaxf(mt, x);
+      }
     }
     // Move the running max when it grows by more than 2^8 (always on the first
     // visible tile).  tcgen05.ld/st are warp-collective, so the O rescale runs
@@ -293,13 +324,15 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
       }
     }
     const float msub = m_use == -INFINITY ? 0.f : m_use;
+    // p = 2^(x - m): one FFMA into the exponent for plain tiles, one FADD otherwise
+    const float sa = plain ? b.scale_log2 : 1.f;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const float p0 = exp2f(s[32 * c + 2 * i] - msub);
-        const float p1 = exp2f(s[32 * c + 2 * i + 1] - msub);
+        const float p0 = fast_exp2(fmaf(s[32 * c + 2 * i], sa, -msub));
+        const float p1 = fast_exp2(fmaf(s[32 * c + 2 * i + 1], sa, -msub));
         l += p0 + p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
