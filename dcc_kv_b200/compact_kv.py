@@ -104,6 +104,18 @@ def build_problem(keys: torch.Tensor, values: torch.Tensor, repr_q: torch.Tensor
     return p
 
 
+def build_launch_count(n_problems: int, dtype_code: int, head_dim: int) -> int:
+    """Kernel launches of one batched build (C-library batch caps: 128 edges per
+    flush; tcgen05 scoring 56 edges per launch; 6 calibration launches)."""
+    n, total = n_problems, 0
+    while n > 0:
+        k = min(n, 128)
+        scoring = 2 * -(-k // 56) if (dtype_code == L.DCC_BF16 and head_dim == 128) else 2
+        total += scoring + 1 + 6
+        n -= k
+    return total
+
+
 def run_build_problems(problems: Sequence[L.dcc_build_problem], head_dim: int, value_dim: int,
                        lambda_beta: float, lambda_value: float, dtype_code: int, device: torch.device,
                        workspace: Optional[torch.Tensor] = None) -> None:

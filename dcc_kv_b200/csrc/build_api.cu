@@ -41,6 +41,11 @@ static void carve(Workspace& ws, const dcc_build_problem& q, int dv, BuildDesc<A
   d.X = ws.take<double>((size_t)q.num_repr * Bp);
   d.Y = ws.take<double>((size_t)q.num_repr * dv);
   d.wv = ws.take<double>((size_t)Bp);
+  d.n_btiles = (int)((Bp + 63) / 64);
+  const size_t parts = q.num_repr < Bp ? (size_t)d.n_btiles * 64 * 64 : 0;
+  d.gpart = ws.take<double>(parts);
+  d.xpart = ws.take<double>(parts);
+  d.W = ws.take<double>((size_t)64 * dv);
 }
 
 static size_t build_ws_bytes(const dcc_build_problem* probs, int n, int dv, int dtype) {

@@ -35,6 +35,11 @@ struct BuildDesc {
   double* X;     // [M, B']  (logits, then X)
   double* Y;     // [M, dv]
   double* wv;    // [B'] NNLS weights, then beta
+  double* gpart; // [n_btiles, 64, 64] partial Gram G G^T per 64-key tile (M < B')
+  double* xpart; // [n_btiles, 64, 64] partial Gram X X^T
+  double* W;     // [64, dv] (X X^T + lam I)^-1 Y
+  int32_t n_btiles;
+  int32_t pad2;
   // per-function entry points: given inputs instead of computed ones
   const void* in_mass;  // [M] block mass (input dtype), replaces the pass-2 sums
   const void* in_beta;  // [B'] logit bias (input dtype), replaces the NNLS
@@ -45,7 +50,7 @@ struct BuildDesc {
 constexpr int kStageBeta = 1;
 constexpr int kStageValues = 2;
 
-constexpr int kBuildCap = 96;
+constexpr int kBuildCap = 128;
 template <typename Acc>
 using BuildBatch = Batch<BuildDesc<Acc>, kBuildCap>;
 

@@ -1,0 +1,402 @@
+// Logit-bias calibration and compact-value regression of the build, FP64.
+//
+// beta (calibration.py:63-94): G = exp(Q^ C_K^T * scale) [M, B'];
+//   M < B' : w = clamp(G^T (G G^T + lam I)^-1 t, 0) -- the push-through form of
+//            the reference's B x B ridge solve clamp(solve(G^T G + lam I, G^T t), 0)
+//            (:44-47): the same vector in exact arithmetic, an M x M system;
+//   B' <= M: the literal B x B solve, then 100 projected-gradient steps (lr
+//            1e-2, ridge toward 1, :54-60);
+//   beta = log(max(w, 1e-6)).
+// values (value_regression.py:38-78): X = softmax(Q^ C_K^T * scale + beta / M),
+//   M < B' : C_V = X^T (X X^T + lam I)^-1 Y ;  B' <= M : (X^T X + lam I)^-1 X^T Y.
+//
+// Six launches; the GEMM-shaped parts run as grids over (64-key tile, problem):
+//   calib_logits  logits, G and partial Grams G_t G_t^T per tile   [tiles x problems]
+//   calib_beta    sum of partial Grams, Cholesky, w, beta           [problems]
+//   calib_x       X = row softmax of (logits + beta / M)            [problems]
+//   calib_xgram   partial Grams X_t X_t^T                           [tiles x problems]
+//   calib_w       Y from the scoring partials, Cholesky, W          [problems]
+//   calib_cv      C_V = X^T W per tile                              [tiles x problems]
+// Partial Grams are summed in tile order, so results do not depend on timing.
+#include "dense_fp64.cuh"
+
+namespace dcc {
+
+constexpr int kCalTile = 64;
+
+template <typename TIn> struct CalStore { using T = float; };  // bf16 / fp32 values are exact in fp32
+template <> struct CalStore<double> { using T = double; };
+
+template <typename Acc>
+__device__ __forceinline__ int cal_bp(const BuildDesc<Acc>& p) {
+  return (int)((int64_t)p.budget < p.L_s ? (int64_t)p.budget : p.L_s);
+}
+
+// 64 x 64 partial Gram of a [64][kLdG] shared tile: out[a][a2] = sum_b Z[a][b] Z[a2][b]
+// (thread owns rows ta + 16 i and columns tb + 16 j, i, j < 4; 256 threads).
+__device__ __forceinline__ void tile_gram(const double* zs, double* out) {
+  const int ta = threadIdx.x & 15, tb = threadIdx.x >> 4;
+  double acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+  for (int c = 0; c < kCalTile; ++c) {
+    double za[4], zb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      za[i] = zs[(ta + 16 * i) * kLdG + c];
+      zb[i] = zs[(tb + 16 * i) * kLdG + c];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = fma(za[i], zb[j], acc[i][j]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) out[(ta + 16 * i) * 64 + tb + 16 * j] = acc[i][j];
+}
+
+// ---- 1. logits, G, partial Gram of G --------------------------------------------------
+template <typename TIn, typename Acc>
+__global__ void __launch_bounds__(256) calib_logits_kernel(const __grid_constant__ BuildBatch<Acc> b,
+                                                           const BuildParams prm) {
+  using ST = typename CalStore<TIn>::T;
+  const BuildDesc<Acc>& p = b.p[blockIdx.y];
+  const int Bp = cal_bp(p), M = p.M, d = prm.d;
+  const int tile = blockIdx.x;
+  if (tile >= p.n_btiles) return;
+  const int b0 = tile * kCalTile;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  const int ld = d + 1;
+  ST* qs = reinterpret_cast<ST*>(smem_raw);                  // [64][d+1]
+  ST* ks = qs + 64 * ld;                                       // [64][d+1]
+  double* gs = reinterpret_cast<double*>(smem_raw + ((2 * 64 * ld * sizeof(ST) + 15) / 16) * 16);  // [64][65]
+  const TIn* rq = static_cast<const TIn*>(p.repr);
+  const TIn* ck = static_cast<const TIn*>(p.out_keys);
+  for (int e = threadIdx.x; e < 64 * d; e += blockDim.x) {
+    const int r = e / d, c = e - r * d;
+    qs[r * ld + c] = r < M ? (ST)to_f64<TIn>(rq[r * d + c]) : (ST)0;
+    ks[r * ld + c] = b0 + r < Bp ? (ST)to_f64<TIn>(ck[(int64_t)(b0 + r) * d + c]) : (ST)0;
+  }
+  __syncthreads();
+  const int ta = threadIdx.x & 15, tb = threadIdx.x >> 4;
+  double acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+  for (int c = 0; c < d; ++c) {
+    double qa[4], kb[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      qa[i] = (double)qs[(ta + 16 * i) * ld + c];
+      kb[i] = (double)ks[(tb + 16 * i) * ld + c];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = fma(qa[i], kb[j], acc[i][j]);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int a = ta + 16 * i;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int bb = tb + 16 * j;
+      const bool ok = a < M && b0 + bb < Bp;
+      const double lg = acc[i][j] * prm.scale;  // (Q^ C_K^T) * scale, calibration.py:84
+      const double g = ok ? exp(lg) : 0.0;
+      if (ok) {
+        p.X[(int64_t)a * Bp + b0 + bb] = lg;
+        p.G[(int64_t)a * Bp + b0 + bb] = g;
+      }
+      gs[a * kLdG + bb] = g;
+    }
+  }
+  if (!(p.stages & kStageBeta) || M >= Bp) return;
+  __syncthreads();
+  tile_gram(gs, p.gpart + (int64_t)tile * 4096);
+}
+
+// ---- 2. beta ---------------------------------------------------------------------------
+template <typename TIn, typename Acc>
+__global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__ BuildBatch<Acc> b,
+                                                         const BuildParams prm) {
+  const BuildDesc<Acc>& p = b.p[blockIdx.x];
+  const int Bp = cal_bp(p), M = p.M;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  double* gram = reinterpret_cast<double*>(smem_raw);  // [64][65]
+  double* gsm = gram + 64 * kLdG;                      // [64][65]
+  double* tv = gsm + 64 * kLdG;                        // [64]
+  double* vv = tv + 64;                                // [64]
+  double* res = vv + 64;                               // [64]
+  // block mass: given, or the pass-2 chunk sums in chunk order
+  for (int a = threadIdx.x; a < 64; a += blockDim.x) {
+    double s = 0.0;
+    if (a < M) {
+      if (p.in_mass)
+        s = load_side<TIn>(p.in_mass, a);
+      else
+        for (int c = 0; c < p.n_chunks; ++c) s += (double)p.massp[(int64_t)c * M + a];
+    }
+    tv[a] = s;
+    if (a < M && p.out_mass) p.out_mass[a] = s;
+  }
+  if (!(p.stages & kStageBeta)) {
+    for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) p.wv[bb] = load_side<TIn>(p.in_beta, bb);
+    return;
+  }
+  __syncthreads();
+  const double lb = prm.lambda_beta;
+  if (M < Bp) {
+    for (int e = threadIdx.x; e < M * M; e += blockDim.x) {
+      const int a = e / M, a2 = e % M;
+      double s = 0.0;
+      for (int t = 0; t < p.n_btiles; ++t) s += p.gpart[(int64_t)t * 4096 + a * 64 + a2];
+      gram[a * kLdG + a2] = s + (a == a2 ? lb : 0.0);
+    }
+    __syncthreads();
+    chol_inplace(gram, kLdG, M);
+    if (threadIdx.x < 64) vv[threadIdx.x] = tv[threadIdx.x];
+    __syncthreads();
+    chol_solve_parallel(gram, kLdG, M, vv, 1, 1);
+    for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) {
+      double w = 0.0;
+      for (int a = 0; a < M; ++a) w = fma(p.G[(int64_t)a * Bp + bb], vv[a], w);
+      p.wv[bb] = w > 0.0 ? w : 0.0;
+    }
+  } else {
+    for (int e = threadIdx.x; e < M * Bp; e += blockDim.x) gsm[(e / Bp) * kLdG + e % Bp] = p.G[e];
+    __syncthreads();
+    gram_cols(gsm, M, Bp, lb, gram);
+    for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) {
+      double s = 0.0;
+      for (int a = 0; a < M; ++a) s = fma(gsm[a * kLdG + bb], tv[a], s);
+      vv[bb] = s;
+    }
+    __syncthreads();
+    chol_inplace(gram, kLdG, Bp);
+    chol_solve_parallel(gram, kLdG, Bp, vv, 1, 1);
+    if (threadIdx.x < Bp) vv[threadIdx.x] = fmax(vv[threadIdx.x], 0.0);
+    __syncthreads();
+    for (int it = 0; it < 100; ++it) {
+      if (threadIdx.x < M) {  // res = G w - t
+        double s = 0.0;
+        for (int bb = 0; bb < Bp; ++bb) s = fma(gsm[threadIdx.x * kLdG + bb], vv[bb], s);
+        res[threadIdx.x] = s - tv[threadIdx.x];
+      }
+      __syncthreads();
+      if (threadIdx.x < Bp) {  // w = max(w - lr (G^T res + lam (w - 1)), 0)
+        double g = 0.0;
+        for (int a = 0; a < M; ++a) g = fma(gsm[a * kLdG + threadIdx.x], res[a], g);
+        g += lb * (vv[threadIdx.x] - 1.0);
+        vv[threadIdx.x] = fmax(vv[threadIdx.x] - 1e-2 * g, 0.0);
+      }
+      __syncthreads();
+    }
+    if (threadIdx.x < Bp) p.wv[threadIdx.x] = vv[threadIdx.x];
+  }
+  __syncthreads();
+  for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) {
+    const double beta = log(fmax(p.wv[bb], 1e-6));
+    p.wv[bb] = beta;
+    if (sizeof(TIn) == 8)
+      static_cast<double*>(p.out_bias)[bb] = beta;
+    else
+      static_cast<float*>(p.out_bias)[bb] = (float)beta;
+  }
+}
+
+// ---- 3. X = softmax_b(logits + beta / M), one warp per row ------------------------------
+template <typename Acc>
+__global__ void __launch_bounds__(256) calib_x_kernel(const __grid_constant__ BuildBatch<Acc> b) {
+  const BuildDesc<Acc>& p = b.p[blockIdx.x];
+  if (!(p.stages & kStageValues)) return;
+  const int Bp = cal_bp(p), M = p.M;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int a = warp; a < M; a += blockDim.x >> 5) {
+    double* xr = p.X + (int64_t)a * Bp;
+    double mx = -INFINITY;
+    for (int bb = lane; bb < Bp; bb += 32) {
+      const double v = xr[bb] + p.wv[bb] / (double)M;  // value_regression.py:72-73
+      xr[bb] = v;
+      mx = fmax(mx, v);
+    }
+    mx = warp_max(mx);
+    double sum = 0.0;
+    for (int bb = lane; bb < Bp; bb += 32) {
+      const double e = exp(xr[bb] - mx);
+      xr[bb] = e;
+      sum += e;
+    }
+    sum = warp_sum(sum);
+    for (int bb = lane; bb < Bp; bb += 32) xr[bb] = xr[bb] / sum;
+  }
+}
+
+// ---- 4. partial Grams of X ---------------------------------------------------------------
+template <typename Acc>
+__global__ void __launch_bounds__(256) calib_xgram_kernel(const __grid_constant__ BuildBatch<Acc> b) {
+  const BuildDesc<Acc>& p = b.p[blockIdx.y];
+  const int Bp = cal_bp(p), M = p.M;
+  const int tile = blockIdx.x;
+  if (!(p.stages & kStageValues) || M >= Bp || tile >= p.n_btiles) return;
+  __shared__ double xs[64 * kLdG];
+  const int b0 = tile * kCalTile;
+  for (int e = threadIdx.x; e < 64 * kCalTile; e += blockDim.x) {
+    const int a = e / kCalTile, bb = e % kCalTile;
+    xs[a * kLdG + bb] = (a < M && b0 + bb < Bp) ? p.X[(int64_t)a * Bp + b0 + bb] : 0.0;
+  }
+  __syncthreads();
+  tile_gram(xs, p.xpart + (int64_t)tile * 4096);
+}
+
+// ---- 5. Y, then W = (X X^T + lam I)^-1 Y   (B' <= M: C_V directly) ----------------------
+template <typename TIn, typename Acc>
+__global__ void __launch_bounds__(256) calib_w_kernel(const __grid_constant__ BuildBatch<Acc> b,
+                                                      const BuildParams prm) {
+  const BuildDesc<Acc>& p = b.p[blockIdx.x];
+  if (!(p.stages & kStageValues)) return;
+  const int Bp = cal_bp(p), M = p.M, dv = prm.dv;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  double* gram = reinterpret_cast<double*>(smem_raw);  // [64][65]
+  double* gsm = gram + 64 * kLdG;                      // [64][65]
+  double* ws = gsm + 64 * kLdG;                        // [64][dv+1]
+  const int ldw = dv + 1;
+  for (int e = threadIdx.x; e < M * dv; e += blockDim.x) {  // Y, chunk order
+    double s = 0.0;
+    for (int c = 0; c < p.n_chunks; ++c) s += (double)p.yp[(int64_t)c * M * dv + e];
+    p.Y[e] = s;
+    ws[(e / dv) * ldw + e % dv] = s;
+  }
+  const double lv = prm.lambda_value;
+  if (M < Bp) {
+    for (int e = threadIdx.x; e < M * M; e += blockDim.x) {
+      const int a = e / M, a2 = e % M;
+      double s = 0.0;
+      for (int t = 0; t < p.n_btiles; ++t) s += p.xpart[(int64_t)t * 4096 + a * 64 + a2];
+      gram[a * kLdG + a2] = s + (a == a2 ? lv : 0.0);
+    }
+    __syncthreads();
+    chol_inplace(gram, kLdG, M);
+    chol_solve_parallel(gram, kLdG, M, ws, ldw, dv);
+    for (int e = threadIdx.x; e < M * dv; e += blockDim.x) p.W[e] = ws[(e / dv) * ldw + e % dv];
+  } else {
+    __syncthreads();
+    for (int e = threadIdx.x; e < M * Bp; e += blockDim.x) gsm[(e / Bp) * kLdG + e % Bp] = p.X[e];
+    __syncthreads();
+    gram_cols(gsm, M, Bp, lv, gram);
+    // R = X^T Y into ws rows [0, Bp) (Bp <= M <= 64 rows; Y is kept in p.Y)
+    __syncthreads();
+    for (int e = threadIdx.x; e < Bp * dv; e += blockDim.x) {
+      const int bb = e / dv, c = e % dv;
+      double s = 0.0;
+      for (int a = 0; a < M; ++a) s = fma(gsm[a * kLdG + bb], p.Y[(int64_t)a * dv + c], s);
+      ws[bb * ldw + c] = s;
+    }
+    __syncthreads();
+    chol_inplace(gram, kLdG, Bp);
+    chol_solve_parallel(gram, kLdG, Bp, ws, ldw, dv);
+    TIn* outv = static_cast<TIn*>(p.out_values);
+    for (int e = threadIdx.x; e < Bp * dv; e += blockDim.x) outv[e] = from_f64<TIn>(ws[(e / dv) * ldw + e % dv]);
+  }
+}
+
+// ---- 6. C_V = X^T W per 64-key tile --------------------------------------------------------
+template <typename TIn, typename Acc>
+__global__ void __launch_bounds__(256) calib_cv_kernel(const __grid_constant__ BuildBatch<Acc> b,
+                                                       const BuildParams prm) {
+  const BuildDesc<Acc>& p = b.p[blockIdx.y];
+  const int Bp = cal_bp(p), M = p.M, dv = prm.dv;
+  const int tile = blockIdx.x;
+  if (!(p.stages & kStageValues) || M >= Bp || tile >= p.n_btiles) return;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  double* xs = reinterpret_cast<double*>(smem_raw);  // [64 a][65]
+  double* wsm = xs + 64 * kLdG;                       // [64 a][dv + 1]
+  const int ldw = dv + 1;
+  const int b0 = tile * kCalTile;
+  for (int e = threadIdx.x; e < 64 * kCalTile; e += blockDim.x) {
+    const int a = e / kCalTile, bb = e % kCalTile;
+    xs[a * kLdG + bb] = (a < M && b0 + bb < Bp) ? p.X[(int64_t)a * Bp + b0 + bb] : 0.0;
+  }
+  for (int e = threadIdx.x; e < 64 * dv; e += blockDim.x) {
+    const int a = e / dv, c = e % dv;
+    wsm[a * ldw + c] = a < M ? p.W[(int64_t)a * dv + c] : 0.0;
+  }
+  __syncthreads();
+  // thread: keys tb + 16 i (i < 4), value columns tc + 16 j (j < 8)
+  const int tc = threadIdx.x & 15, tb = threadIdx.x >> 4;
+  TIn* outv = static_cast<TIn*>(p.out_values);
+  for (int c0 = 0; c0 < dv; c0 += 128) {
+    double acc[4][8];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.0;
+    for (int a = 0; a < M; ++a) {
+      double xv[4], wv[8];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) xv[i] = xs[a * kLdG + tb + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = c0 + tc + 16 * j;
+        wv[j] = c < dv ? wsm[a * ldw + c] : 0.0;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[i][j] = fma(xv[i], wv[j], acc[i][j]);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int bb = b0 + tb + 16 * i;
+      if (bb >= Bp) continue;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int c = c0 + tc + 16 * j;
+        if (c < dv) outv[(int64_t)bb * dv + c] = from_f64<TIn>(acc[i][j]);
+      }
+    }
+  }
+}
+
+template <typename TIn, typename Acc>
+int launch_calibrate(const BuildBatch<Acc>& b, const BuildParams& prm, cudaStream_t st) {
+  using ST = typename CalStore<TIn>::T;
+  int tmax = 1;
+  for (int i = 0; i < b.n; ++i) tmax = b.p[i].n_btiles > tmax ? b.p[i].n_btiles : tmax;
+  const size_t smem1 = align_up(2 * 64 * (size_t)(prm.d + 1) * sizeof(ST), 16) + 64 * kLdG * sizeof(double);
+  const size_t smem5 = (2 * 64 * kLdG + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
+  const size_t smem6 = (64 * kLdG + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
+  const size_t smem2 = (2 * 64 * kLdG + 3 * 64) * sizeof(double);
+  auto k1 = calib_logits_kernel<TIn, Acc>;
+  auto k2 = calib_beta_kernel<TIn, Acc>;
+  auto k5 = calib_w_kernel<TIn, Acc>;
+  auto k6 = calib_cv_kernel<TIn, Acc>;
+  DCC_CHECK(check_cuda(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1), "calib smem"));
+  DCC_CHECK(check_cuda(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2), "calib smem"));
+  DCC_CHECK(check_cuda(cudaFuncSetAttribute(k5, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem5), "calib smem"));
+  DCC_CHECK(check_cuda(cudaFuncSetAttribute(k6, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem6), "calib smem"));
+  const dim3 tiles(tmax, b.n);
+  k1<<<tiles, 256, smem1, st>>>(b, prm);
+  DCC_CHECK(check_launch("calib_logits"));
+  k2<<<b.n, 256, smem2, st>>>(b, prm);
+  DCC_CHECK(check_launch("calib_beta"));
+  calib_x_kernel<Acc><<<b.n, 256, 0, st>>>(b);
+  DCC_CHECK(check_launch("calib_x"));
+  calib_xgram_kernel<Acc><<<tiles, 256, 0, st>>>(b);
+  DCC_CHECK(check_launch("calib_xgram"));
+  k5<<<b.n, 256, smem5, st>>>(b, prm);
+  DCC_CHECK(check_launch("calib_w"));
+  k6<<<tiles, 256, smem6, st>>>(b, prm);
+  return check_launch("calib_cv");
+}
+
+template int launch_calibrate<float, double>(const BuildBatch<double>&, const BuildParams&, cudaStream_t);
+template int launch_calibrate<double, double>(const BuildBatch<double>&, const BuildParams&, cudaStream_t);
+template int launch_calibrate<__nv_bfloat16, float>(const BuildBatch<float>&, const BuildParams&, cudaStream_t);
+
+}  // namespace dcc

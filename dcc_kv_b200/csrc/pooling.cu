@@ -49,62 +49,56 @@ __device__ __forceinline__ int64_t set_row_offset(const SetDesc& s, int64_t i) {
 }
 
 // ---- projection: normed[i] = n(n(Q_i P^T)),  n(z) = z / (||z|| + 1e-8) ------
-// 64 rows per CTA, 4 threads per row (adjacent lanes), each computing DPP/4
-// projected coordinates from a shared-memory copy of the rows and of P.
+// One thread per query row holds all DPP projected coordinates in registers.
+// P[k][c] = +-mag, so z_k = sum_c +-(q_c * mag): q_c * mag is exact in FP64
+// for bf16 / fp32 queries (as in the reference's FP64 matmul), only the
+// summation order differs.  Column c's signs sit in one 64-bit word.
+template <typename T>
+__device__ __forceinline__ double load_row_elem(const T* q, int c) { return to_f64<T>(q[c]); }
+
 template <typename T, int DPP>
-__global__ void __launch_bounds__(256) project_kernel(const __grid_constant__ SetBatch b,
+__global__ void __launch_bounds__(128) project_kernel(const __grid_constant__ SetBatch b,
                                                       const __grid_constant__ ProjBits proj, int d,
                                                       int dp) {
-  extern __shared__ double smem[];
+  __shared__ unsigned long long colsign[256];
   const SetDesc& s = b.p[blockIdx.y];
-  const int ld = d + 1;                 // padded row stride (bank spread)
-  double* qs = smem;                    // [64, d + 1]
-  double* ps = smem + 64 * ld;          // [DPP, d]
-  const int64_t row0 = (int64_t)blockIdx.x * 64;
-  if (row0 >= s.n) return;
-  for (int e = threadIdx.x; e < DPP * d; e += blockDim.x) {
-    const int k = e / d;
-    const int bit = k * d + (e - k * d);
-    const bool pos = (proj.bits[bit >> 5] >> (bit & 31)) & 1u;
-    ps[e] = k < dp ? (double)(pos ? proj.mag : -proj.mag) : 0.0;
-  }
-  const T* q = static_cast<const T*>(s.q);
-  for (int e = threadIdx.x; e < 64 * d; e += blockDim.x) {
-    const int r = e / d, c = e - r * d;
-    const int64_t i = row0 + r;
-    qs[r * ld + c] = i < s.n ? to_f64<T>(q[set_row_offset(s, i) + c]) : 0.0;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    unsigned long long w = 0;
+    for (int k = 0; k < dp; ++k) {
+      const int bit = k * d + c;
+      if ((proj.bits[bit >> 5] >> (bit & 31)) & 1u) w |= 1ull << k;
+    }
+    colsign[c] = w;
   }
   __syncthreads();
-  const int r = threadIdx.x >> 2, part = threadIdx.x & 3;
-  constexpr int KP = DPP / 4;
-  double z[KP];
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= s.n) return;
+  const T* q = static_cast<const T*>(s.q) + set_row_offset(s, i);
+  const double mag = (double)proj.mag;
+  double z[DPP];
 #pragma unroll
-  for (int k = 0; k < KP; ++k) z[k] = 0.0;
+  for (int k = 0; k < DPP; ++k) z[k] = 0.0;
   for (int c = 0; c < d; ++c) {
-    const double qv = qs[r * ld + c];
+    const double qp = load_row_elem<T>(q, c) * mag;
+    const unsigned long long w = colsign[c];
 #pragma unroll
-    for (int k = 0; k < KP; ++k) z[k] = fma(qv, ps[(part * KP + k) * d + c], z[k]);
+    for (int k = 0; k < DPP; ++k) {
+      if (k < dp) z[k] += ((w >> k) & 1ull) ? qp : -qp;
+    }
   }
   double ss = 0.0;
 #pragma unroll
-  for (int k = 0; k < KP; ++k) ss = fma(z[k], z[k], ss);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
+  for (int k = 0; k < DPP; ++k) ss = fma(z[k], z[k], ss);
   double inv = 1.0 / (sqrt(ss) + 1e-8);
   ss = 0.0;
 #pragma unroll
-  for (int k = 0; k < KP; ++k) {
+  for (int k = 0; k < DPP; ++k) {
     z[k] = z[k] * inv;  // z / (||z|| + 1e-8), representative_query.py:108
     ss = fma(z[k], z[k], ss);
   }
-  ss += __shfl_xor_sync(0xffffffffu, ss, 1);
-  ss += __shfl_xor_sync(0xffffffffu, ss, 2);
   inv = 1.0 / (sqrt(ss) + 1e-8);  // normalised again inside FPS, :63
-  const int64_t i = row0 + r;
-  if (i < s.n) {
 #pragma unroll
-    for (int k = 0; k < KP; ++k) s.normed[i * DPP + part * KP + k] = z[k] * inv;
-  }
+  for (int k = 0; k < DPP; ++k) s.normed[i * DPP + k] = z[k] * inv;
 }
 
 struct Cand {
@@ -346,23 +340,14 @@ static int run_pooling(SetBatch& b, int d, int M, int dp, const ProjBits& proj, 
                        cudaStream_t st) {
   const int dpp = dpp_for(dp);
   // projection
-  const int blocks_x = (max_n + 63) / 64;
-  const size_t smem = (size_t)(64 * (d + 1) + dpp * d) * sizeof(double);
+  const int blocks_x = (max_n + 127) / 128;
   dim3 grid(blocks_x, b.n);
-#define DCC_PROJ(P)                                                                          \
-  do {                                                                                       \
-    auto k = project_kernel<T, P>;                                                           \
-    DCC_CHECK(check_cuda(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, \
-                                              (int)smem), "project smem"));                  \
-    k<<<grid, 256, smem, st>>>(b, proj, d, dp);                                             \
-  } while (0)
   switch (dpp) {
-    case 8: DCC_PROJ(8); break;
-    case 16: DCC_PROJ(16); break;
-    case 32: DCC_PROJ(32); break;
-    default: DCC_PROJ(64); break;
+    case 8: project_kernel<T, 8><<<grid, 128, 0, st>>>(b, proj, d, dp); break;
+    case 16: project_kernel<T, 16><<<grid, 128, 0, st>>>(b, proj, d, dp); break;
+    case 32: project_kernel<T, 32><<<grid, 128, 0, st>>>(b, proj, d, dp); break;
+    default: project_kernel<T, 64><<<grid, 128, 0, st>>>(b, proj, d, dp); break;
   }
-#undef DCC_PROJ
   DCC_CHECK(check_launch("project"));
   switch (dpp) {
     case 8: return run_fps<T, 8>(b, M, d, max_n, st);

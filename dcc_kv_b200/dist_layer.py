@@ -31,7 +31,7 @@ import torch.distributed as dist
 
 from . import _lib as L
 from .attention import attn_problem, kv_segment, run_attention
-from .compact_kv import build_problem, run_build_problems
+from .compact_kv import build_launch_count, build_problem, run_build_problems
 from .layer import Budgets, budget_table
 from .online_softmax import merge_lse
 from .representative_query import query_set, select_query_sets
@@ -229,5 +229,5 @@ class DistributedDccKvLayer:
     def launches_per_forward(self) -> int:
         sets = len(self.sets)
         pool = 0 if sets == 0 else 2 * -(-sets // 64)
-        return (pool + 4 * -(-len(self.build) // 96) + -(-len(self.local_problems) // 8)
+        return (pool + build_launch_count(len(self.build), self.code, self.d) + -(-len(self.local_problems) // 8)
                 + -(-len(self.compact_problems) // 8) + len(self.merge_rows))

@@ -28,7 +28,7 @@ import torch
 from . import _lib as L
 from .attention import attn_problem, kv_segment, run_attention
 from .calibration import side_dtype
-from .compact_kv import build_problem, run_build_problems
+from .compact_kv import build_launch_count, build_problem, run_build_problems
 from .online_softmax import merge_lse
 from .representative_query import query_set, select_query_sets
 
@@ -162,7 +162,7 @@ class DccKvSyncLayer:
         64 query sets, 96 build edges, 8 tcgen05 attention problems per launch)."""
         sets = len(self.sets)
         pool = 0 if sets == 0 else (2 if self.m_eff < self.group * self.window else 1) * -(-sets // 64)
-        build = 4 * -(-len(self.build) // 96)
+        build = build_launch_count(len(self.build), self.code, self.d)
         attn = -(-len(self.local_problems) // 8) + -(-len(self.compact_problems) // 8)
         return pool + build + attn + (1 if self.nb > 1 else 0)
 
