@@ -78,7 +78,7 @@ struct Smem {
   unsigned char q[2][kTileBytes];    // head A, head B
   unsigned char k[2][kTileBytes];    // stages
   unsigned char v[2][kTileBytes];
-  float bias[2][kKeys];
+  __align__(16) float bias[2][kKeys];
   uint64_t bar_q, bar_k[2], bar_v[2], bar_bias[2], bar_empty[2], bar_s[2], bar_p[2], bar_o[2];
   uint32_t tmem;
 };
@@ -281,13 +281,27 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     const int64_t lim = causal ? q_row + p.causal_offset : t.kend - 1;  // last visible key
     const int64_t lim2 = lim < t.kend - 1 ? lim : t.kend - 1;
     const int nvis = (int)(lim2 - t.t0 + 1 < 0 ? 0 : (lim2 - t.t0 + 1 > 128 ? 128 : lim2 - t.t0 + 1));
-    const bool plain = __all_sync(0xffffffffu, nvis == 128) && !p.seg[t.seg].bias;
+    const bool full = __all_sync(0xffffffffu, nvis == 128) != 0;
+    const bool biased = p.seg[t.seg].bias != nullptr;
+    const bool plain = full && !biased;
     float mt = -INFINITY;
     if (plain) {
       // whole tile visible, no bias: max of the raw scores, scaled once
 #pragma unroll
       for (int c = 0; c < 128; ++c) mt = fmaxf(mt, s[c]);
       mt *= b.scale_log2;
+    } else if (full) {
+      // whole tile visible with a per-key bias (log2 units, 16-byte shared loads)
+      const float4* bv = reinterpret_cast<const float4*>(sm.bias[st]);
+#pragma unroll
+      for (int c4 = 0; c4 < 32; ++c4) {
+        const float4 bb = bv[c4];
+        s[4 * c4 + 0] = fmaf(s[4 * c4 + 0], b.scale_log2, bb.x);
+        s[4 * c4 + 1] = fmaf(s[4 * c4 + 1], b.scale_log2, bb.y);
+        s[4 * c4 + 2] = fmaf(s[4 * c4 + 2], b.scale_log2, bb.z);
+        s[4 * c4 + 3] = fmaf(s[4 * c4 + 3], b.scale_log2, bb.w);
+        mt = fmaxf(fmaxf(mt, fmaxf(s[4 * c4 + 0], s[4 * c4 + 1])), fmaxf(s[4 * c4 + 2], s[4 * c4 + 3]));
+      }
     } else {
 #pragma unroll
       for (int c = 0; c < 128; ++c) {

@@ -14,9 +14,9 @@ All buffers and kernel descriptors are built once per shape; ``forward``
 only enqueues kernels on the current stream:
     1 projection + 1 FPS launch       (all (destination, KV head) sets)
     4 build launches per <=128 edges  (score stats, score probs, top-k, solves)
-    1 local causal attention launch   (all blocks)
-    1 compact attention launch        (all destinations, bias per key)
-    1 merge launch                    (in place into the local output)
+    1 attention launch: per block its causal local segment followed by its
+      compact segment with the logit bias, one online softmax over both (the
+      merge of dcc_kv_sync_cpu.py:81-84 happens inside the kernel)
 """
 from __future__ import annotations
 
@@ -29,7 +29,6 @@ from . import _lib as L
 from .attention import attn_problem, kv_segment, run_attention
 from .calibration import side_dtype
 from .compact_kv import build_launch_count, build_problem, run_build_problems
-from .online_softmax import merge_lse
 from .representative_query import query_set, select_query_sets
 
 Budgets = Union[int, Dict[Tuple[int, int], int]]
@@ -81,10 +80,7 @@ class DccKvSyncLayer:
         self.cv = [torch.empty(n_kv_heads, t, d, dtype=dtype, device=dev) for t in self.total]
         self.cb = [torch.empty(n_kv_heads, t, dtype=sd, device=dev) for t in self.total]
         self.ci = [torch.empty(n_kv_heads, t, dtype=torch.int64, device=dev) for t in self.total]
-        self.o_loc = torch.empty(n_blocks, n_q_heads, block_len, d, dtype=dtype, device=dev)
-        self.lse_loc = torch.empty(n_blocks, n_q_heads, block_len, dtype=torch.float32, device=dev)
-        self.o_c = torch.empty(max(n_blocks - 1, 1), n_q_heads, block_len, d, dtype=dtype, device=dev)
-        self.lse_c = torch.empty(max(n_blocks - 1, 1), n_q_heads, block_len, dtype=torch.float32, device=dev)
+        self.out = torch.empty(n_blocks, n_q_heads, block_len, d, dtype=dtype, device=dev)
         self._bound = None
         self._ws = None
         # optional (start, end) CUDA events per step around the local-attention launch
@@ -117,11 +113,15 @@ class DccKvSyncLayer:
             arr = (L.dcc_build_problem * n)(*self.build)
             need = L.lib().dcc_build_compact_kv_workspace_bytes(arr, n, self.d, self.d, self.code)
             self._ws = L.workspace(need, self.device)
-        self.local_problems = [attn_problem(q[b], self.o_loc[b], self.lse_loc[b], [kv_segment(k[b], v[b])], causal=True)
-                      for b in range(self.nb)]
-        self.compact_problems = [attn_problem(q[r], self.o_c[r - 1], self.lse_c[r - 1],
-                                              [kv_segment(self.ck[r], self.cv[r], self.cb[r])])
-                                 for r in range(1, self.nb) if self.total[r] > 0]
+        # one attention problem per block: its causal local segment, then (for r >= 1)
+        # the concatenated compact blocks with their logit bias -- the online softmax
+        # runs over both in one pass, so no separate merge is needed
+        self.attn_problems = []
+        for b in range(self.nb):
+            segs = [kv_segment(k[b], v[b])]
+            if b > 0 and self.total[b] > 0:
+                segs.append(kv_segment(self.ck[b], self.cv[b], self.cb[b]))
+            self.attn_problems.append(attn_problem(q[b], self.out[b], None, segs, causal=True))
         self._bound = key
 
     def check_inputs(self, q, k, v):
@@ -146,14 +146,10 @@ class DccKvSyncLayer:
         ev = self.timing_events[self.timing_index] if self.timing_events else None
         if ev is not None:
             ev[0].record(torch.cuda.current_stream(dev))
-        run_attention(self.local_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
+        run_attention(self.attn_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
         if ev is not None:
             ev[1].record(torch.cuda.current_stream(dev))
-        run_attention(self.compact_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
-        if self.nb > 1:
-            merge_lse([self.o_loc[1:], self.o_c[: self.nb - 1]], [self.lse_loc[1:], self.lse_c[: self.nb - 1]],
-                      out=self.o_loc[1:], want_lse=False)
-        return self.o_loc
+        return self.out
 
     __call__ = forward
 
@@ -163,8 +159,8 @@ class DccKvSyncLayer:
         sets = len(self.sets)
         pool = 0 if sets == 0 else (2 if self.m_eff < self.group * self.window else 1) * -(-sets // 64)
         build = build_launch_count(len(self.build), self.code, self.d)
-        attn = -(-len(self.local_problems) // 8) + -(-len(self.compact_problems) // 8)
-        return pool + build + attn + (1 if self.nb > 1 else 0)
+        attn = -(-len(self.attn_problems) // 8)
+        return pool + build + attn
 
     def compact(self, s: int, r: int, h: int):
         """The CompactKV C_{s->r} of KV head h from the last forward."""
