@@ -7,13 +7,15 @@ balances across ranks).  One forward on every rank:
   0. pooling: representative queries of the local destination blocks
      (FP64 FPS), then ``all_gather`` of the [n_local, H_kv, M, d] tensors
      (the only collective before the exchange; ~128 KB per rank);
+     steps 0-2 run on a high-priority side stream;
   1. builds: every local source s builds C_{s->r} for every r > s, written
      straight into the wire layout (var_len_msg.EdgeLayout) of a
      per-destination-rank send buffer (edges between co-resident blocks go
      to a local buffer and never touch NCCL);
   2. exchange: one NCCL all-to-allv of the byte buffers on a side stream,
      sizes known from the shared budget table (no size round trip);
-  3. local causal attention on the main stream, overlapped with (2);
+  3. local causal attention on the main stream from the start, overlapped
+     with (0)-(2);
   4. compact attention with logit bias, one KV segment per source edge,
      read in place from the receive / local buffers;
   5. online-softmax merge into the local output.
@@ -146,7 +148,11 @@ class DistributedDccKvLayer:
         self.lse_loc = torch.empty(self.n_local, n_q_heads, block_len, dtype=torch.float32, device=dev)
         self.o_c = torch.empty_like(self.o_loc)
         self.lse_c = torch.empty_like(self.lse_loc)
-        self.comm_stream = torch.cuda.Stream(device=dev)
+        # pooling, the gather, the builds and the exchange run on a high-priority
+        # side stream, so their kernels are dispatched ahead of the local
+        # attention that fills the GPU meanwhile on the main stream
+        lo, hi = torch.cuda.Stream.priority_range()
+        self.comm_stream = torch.cuda.Stream(device=dev, priority=hi)
         self._bound = None
         self.timing_events = None
         self.timing_index = 0
@@ -200,16 +206,16 @@ class DistributedDccKvLayer:
         self._bind(q, k, v)
         dev = self.device
         main = torch.cuda.current_stream(dev)
-        select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
-        dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.group)
-        run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
-        # exchange on the side stream, local attention meanwhile
-        self.comm_stream.wait_stream(main)
-        with torch.cuda.stream(self.comm_stream):
-            dist.all_to_all_single(self.recv_buf[: sum(self.recv_splits)] if sum(self.recv_splits) else self.recv_buf[:0],
-                                   self.send_buf[: sum(self.send_splits)] if sum(self.send_splits) else self.send_buf[:0],
-                                   output_split_sizes=self.recv_splits, input_split_sizes=self.send_splits,
-                                   group=self.group)
+        side = self.comm_stream
+        side.wait_stream(main)  # inputs written, previous step's buffers released
+        with torch.cuda.stream(side):
+            select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
+            dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.group)
+            run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
+            ns, nr = sum(self.send_splits), sum(self.recv_splits)
+            dist.all_to_all_single(self.recv_buf[:nr], self.send_buf[:ns], output_split_sizes=self.recv_splits,
+                                   input_split_sizes=self.send_splits, group=self.group)
+        # local causal attention meanwhile, on the main stream
         scale = 1.0 / math.sqrt(self.d)
         ev = self.timing_events[self.timing_index] if self.timing_events else None
         if ev is not None:
@@ -217,7 +223,7 @@ class DistributedDccKvLayer:
         run_attention(self.local_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
         if ev is not None:
             ev[1].record(main)
-        main.wait_stream(self.comm_stream)
+        main.wait_stream(side)
         run_attention(self.compact_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
         for li in self.merge_rows:
             merge_lse([self.o_loc[li], self.o_c[li]], [self.lse_loc[li], self.lse_c[li]], out=self.o_loc[li],
