@@ -324,6 +324,27 @@ def _teardown(ws: int) -> None:
         dist.destroy_process_group()
 
 
+def profile_attention(args):
+    """One fused attention launch of the last destination block (16384 causal
+    local keys + 7 x 1024 compact keys with bias, 32/8 heads, d 128, bf16;
+    ~250 MB on the device) after one warm-up launch: the small case for ncu."""
+    import math as _m
+    from dcc_kv_b200.attention import attn_problem, kv_segment, run_attention
+    from dcc_kv_b200.workloads import gqa_block
+    dev = torch.device("cuda", 0)
+    q, k, v = gqa_block(HQ, HKV, BLOCK_LEN, D, 1007, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ck = torch.randn(HKV, 7 * BUDGET, D, generator=g, device="cuda").to(torch.bfloat16)
+    cv = torch.randn(HKV, 7 * BUDGET, D, generator=g, device="cuda").to(torch.bfloat16)
+    cb = torch.randn(HKV, 7 * BUDGET, generator=g, device="cuda")
+    o = torch.empty_like(q)
+    prob = attn_problem(q, o, None, [kv_segment(k, v), kv_segment(ck, cv, cb)], causal=True)
+    for _ in range(2):
+        run_attention([prob], HQ, HKV, D, 1.0 / _m.sqrt(D), 1, dev)
+    torch.cuda.synchronize()
+    print("profiled attention launch done", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -331,8 +352,12 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--profile-attention", action="store_true",
+                    help="run two attention launches of one block (small case for ncu) and exit")
     args = ap.parse_args()
-    if args.impl == "reference":
+    if args.profile_attention:
+        profile_attention(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_gpu(args)

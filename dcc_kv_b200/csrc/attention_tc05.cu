@@ -284,12 +284,14 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     const bool full = __all_sync(0xffffffffu, nvis == 128) != 0;
     const bool biased = p.seg[t.seg].bias != nullptr;
     const bool plain = full && !biased;
-    float mt = -INFINITY;
+    // row max over 8 independent chains (a single 128-long chain stalls on latency)
+    float mx[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
     if (plain) {
       // whole tile visible, no bias: max of the raw scores, scaled once
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mt = fmaxf(mt, s[c]);
-      mt *= b.scale_log2;
+      for (int c = 0; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
     } else if (full) {
       // whole tile visible with a per-key bias (log2 units, 16-byte shared loads)
       const float4* bv = reinterpret_cast<const float4*>(sm.bias[st]);
@@ -300,16 +302,18 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
         s[4 * c4 + 1] = fmaf(s[4 * c4 + 1], b.scale_log2, bb.y);
         s[4 * c4 + 2] = fmaf(s[4 * c4 + 2], b.scale_log2, bb.z);
         s[4 * c4 + 3] = fmaf(s[4 * c4 + 3], b.scale_log2, bb.w);
-        mt = fmaxf(fmaxf(mt, fmaxf(s[4 * c4 + 0], s[4 * c4 + 1])), fmaxf(s[4 * c4 + 2], s[4 * c4 + 3]));
       }
+#pragma unroll
+      for (int c = 0; c < 128; ++c) mx[c & 7] = fmaxf(mx[c & 7], s[c]);
     } else {
 #pragma unroll
       for (int c = 0; c < 128; ++c) {
-        const float x = c < nvis ? fmaf(s[c], b.scale_log2, sm.bias[st][c]) : -INFINITY;
-        s[c] = x;
-        mt = fmaxf(mt, x);
+        s[c] = c < nvis ? fmaf(s[c], b.scale_log2, sm.bias[st][c]) : -INFINITY;
+        mx[c & 7] = fmaxf(mx[c & 7], s[c]);
       }
     }
+    float mt = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])), fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
+    if (plain) mt *= b.scale_log2;
     // Move the running max when it grows by more than 2^8 (always on the first
     // visible tile).  tcgen05.ld/st are warp-collective, so the O rescale runs
     // for the whole warp when any of its rows needs it (others scale by 1).
@@ -340,6 +344,9 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     const float msub = m_use == -INFINITY ? 0.f : m_use;
     // p = 2^(x - m): one FFMA into the exponent for plain tiles, one FADD otherwise
     const float sa = plain ? b.scale_log2 : 1.f;
+    float ls[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ls[i] = 0.f;
 #pragma unroll
     for (int c = 0; c < 4; ++c) {
       uint32_t pk[16];
@@ -347,11 +354,13 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
       for (int i = 0; i < 16; ++i) {
         const float p0 = fast_exp2(fmaf(s[32 * c + 2 * i], sa, -msub));
         const float p1 = fast_exp2(fmaf(s[32 * c + 2 * i + 1], sa, -msub));
-        l += p0 + p1;
+        ls[(2 * i) & 7] += p0;
+        ls[(2 * i + 1) & 7] += p1;
         pk[i] = pack_bf16x2(p0, p1);
       }
       tmem_st16(tm + lane_off + s_col + 16 * c, pk);
     }
+    l += ((ls[0] + ls[1]) + (ls[2] + ls[3])) + ((ls[4] + ls[5]) + (ls[6] + ls[7]));
     tmem_wait_st();
     tc_fence_before();
     mbar_arrive(&sm.bar_p[role]);
