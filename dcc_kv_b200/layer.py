@@ -11,12 +11,15 @@ added at full weight; the partial outputs are merged by online softmax.
 Layout (HBM): block-major, head-major, contiguous --
     q [n_blocks, H_q, L, d], k / v [n_blocks, H_kv, L, d], out like q.
 All buffers and kernel descriptors are built once per shape; ``forward``
-only enqueues kernels on the current stream:
+on device inputs only enqueues kernels on the current stream:
     1 projection + 1 FPS launch       (all (destination, KV head) sets)
-    4 build launches per <=128 edges  (score stats, score probs, top-k, solves)
+    9 build launches per <=128 edges  (score stats, score probs, top-k, six
+                                       calibration launches)
     1 attention launch: per block its causal local segment followed by its
       compact segment with the logit bias, one online softmax over both (the
       merge of dcc_kv_sync_cpu.py:81-84 happens inside the kernel)
+On host inputs the same kernels run block by block, pipelined with the
+host <-> device copies (``_forward_host``).
 """
 from __future__ import annotations
 
@@ -83,6 +86,8 @@ class DccKvSyncLayer:
         self.out = torch.empty(n_blocks, n_q_heads, block_len, d, dtype=dtype, device=dev)
         self._bound = None
         self._ws = None
+        self._host_out = None
+        self._staging = None
         # optional (start, end) CUDA events per step around the local-attention launch
         self.timing_events = None
         self.timing_index = 0
@@ -92,14 +97,23 @@ class DccKvSyncLayer:
         key = (q.data_ptr(), k.data_ptr(), v.data_ptr())
         if self._bound == key:
             return
+        if self._staging is not None:
+            # the workspace below may still be in use by the side stream
+            torch.cuda.current_stream(self.device).wait_stream(self._streams[1])
         g = self.group
         self.sets = []
+        # per destination block r: its query sets and the edges s -> r, as
+        # slices of the batched lists (the host-buffer path runs them block by block)
+        self.sets_of = [slice(0, 0)]
+        self.build_of = [slice(0, 0)]
         for r in range(1, self.nb):
+            self.sets_of.append(slice(len(self.sets), len(self.sets) + self.hkv))
             for h in range(self.hkv):
                 self.sets.append(query_set(q[r, h * g], self.repr[r, h], self.repr_idx[r, h], n_seg=g,
                                            seg_rows=self.window, seg_stride=q.stride(1), row_stride=q.stride(2)))
         self.build = []
         for r in range(1, self.nb):
+            self.build_of.append(slice(len(self.build), len(self.build) + r * self.hkv))
             for s in range(r):
                 b = self.budgets[(s, r)]
                 bp = min(b, self.L)
@@ -108,10 +122,14 @@ class DccKvSyncLayer:
                     self.build.append(build_problem(
                         k[s, h], v[s, h], self.repr[r, h], b, self.ck[r][h, o:o + bp], self.cv[r][h, o:o + bp],
                         self.cb[r][h, o:o + bp], self.ci[r][h, o:o + bp], num_repr=self.m_eff))
-        n = len(self.build)
-        if n:
-            arr = (L.dcc_build_problem * n)(*self.build)
-            need = L.lib().dcc_build_compact_kv_workspace_bytes(arr, n, self.d, self.d, self.code)
+        need = 0
+        for part in [slice(0, len(self.build))] + self.build_of[1:]:
+            probs = self.build[part]
+            if probs:
+                arr = (L.dcc_build_problem * len(probs))(*probs)
+                need = max(need, L.lib().dcc_build_compact_kv_workspace_bytes(arr, len(probs), self.d, self.d,
+                                                                              self.code))
+        if need:
             self._ws = L.workspace(need, self.device)
         # one attention problem per block: its causal local segment, then (for r >= 1)
         # the concatenated compact blocks with their logit bias -- the online softmax
@@ -134,9 +152,17 @@ class DccKvSyncLayer:
             if t.dtype != self.dtype or not t.is_contiguous():
                 raise ValueError(f"inputs must be contiguous {self.dtype}")
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
-        """q [nb, H_q, L, d], k / v [nb, H_kv, L, d] -> out [nb, H_q, L, d]
-        (the returned tensor is an internal buffer, reused by the next call)."""
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """q [nb, H_q, L, d], k / v [nb, H_kv, L, d] -> out [nb, H_q, L, d].
+
+        Device inputs: the returned tensor is an internal buffer, reused by
+        the next call.  Host inputs (CPU tensors, pinned for overlap): the
+        call streams them in block by block and returns ``out`` (or an
+        internal pinned host buffer); like a ``non_blocking`` copy it is
+        complete once the current stream is synchronized."""
+        if not q.is_cuda:
+            return self._forward_host(q, k, v, out)
         self.check_inputs(q, k, v)
         self._bind(q, k, v)
         dev = self.device
@@ -152,6 +178,74 @@ class DccKvSyncLayer:
         return self.out
 
     __call__ = forward
+
+    def _forward_host(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                      out: Optional[torch.Tensor]) -> torch.Tensor:
+        """Host buffers in and out, pipelined per block over four streams:
+        copy-in of block b (h2d) || pooling of b + builds s -> b (high-priority
+        side stream) || attention of b (current stream) || copy-out of block
+        b (d2h).  Block b's builds only need the keys / values of blocks
+        s < b, which arrived earlier, so the copies hide behind the compute."""
+        exp_q = (self.nb, self.hq, self.L, self.d)
+        exp_kv = (self.nb, self.hkv, self.L, self.d)
+        for t, shp in ((q, exp_q), (k, exp_kv), (v, exp_kv)):
+            if t.is_cuda or tuple(t.shape) != shp or t.dtype != self.dtype or not t.is_contiguous():
+                raise ValueError(f"host inputs must be contiguous CPU {self.dtype} tensors of shape "
+                                 f"q {exp_q}, k/v {exp_kv}")
+        if out is None:
+            if self._host_out is None:
+                self._host_out = torch.empty(exp_q, dtype=self.dtype).pin_memory()
+            out = self._host_out
+        elif out.is_cuda or tuple(out.shape) != exp_q or out.dtype != self.dtype or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous CPU {self.dtype} tensor of shape {exp_q}")
+        dev = self.device
+        if self._staging is None:
+            self._staging = (torch.empty(exp_q, dtype=self.dtype, device=dev),
+                             torch.empty(exp_kv, dtype=self.dtype, device=dev),
+                             torch.empty(exp_kv, dtype=self.dtype, device=dev))
+            lo, hi = torch.cuda.Stream.priority_range()
+            self._streams = tuple(torch.cuda.Stream(device=dev, priority=p) for p in (0, hi, 0))
+            self._events = [[torch.cuda.Event() for _ in range(self.nb)] for _ in range(4)]
+            self._compute_done = None
+        dq, dk_, dv = self._staging
+        self._bind(dq, dk_, dv)
+        h2d, side, d2h = self._streams
+        copied, built, attended, drained = self._events
+        main = torch.cuda.current_stream(dev)
+        # the previous call's kernels must be done reading the staging buffers
+        if self._compute_done is None:
+            self._compute_done = torch.cuda.Event()
+            h2d.wait_stream(main)
+        else:
+            h2d.wait_event(self._compute_done)
+        with torch.cuda.stream(h2d):
+            for b in range(self.nb):
+                dq[b].copy_(q[b], non_blocking=True)
+                dk_[b].copy_(k[b], non_blocking=True)
+                dv[b].copy_(v[b], non_blocking=True)
+                copied[b].record(h2d)
+        scale = 1.0 / math.sqrt(self.d)
+        side.wait_stream(main)
+        for b in range(self.nb):
+            if b > 0:
+                side.wait_event(copied[b])
+                with torch.cuda.stream(side):
+                    select_query_sets(self.sets[self.sets_of[b]], self.d, self.M, self.dp, self.seed, self.code, dev)
+                    run_build_problems(self.build[self.build_of[b]], self.d, self.d, self.lb, self.lv, self.code,
+                                       dev, self._ws)
+                built[b].record(side)
+                main.wait_event(built[b])
+            main.wait_event(copied[b])
+            main.wait_event(drained[b])  # the previous call's copy-out of this block
+            run_attention([self.attn_problems[b]], self.hq, self.hkv, self.d, scale, self.code, dev)
+            attended[b].record(main)
+            d2h.wait_event(attended[b])
+            with torch.cuda.stream(d2h):
+                out[b].copy_(self.out[b], non_blocking=True)
+                drained[b].record(d2h)
+        self._compute_done.record(main)
+        main.wait_stream(d2h)
+        return out
 
     def launches_per_forward(self) -> int:
         """Kernel launches one forward enqueues (batch caps of the C library:

@@ -99,3 +99,27 @@ def test_layer_full_128k_bf16_sampled():
         got = np64(out[r][:, rows[r]])
         assert rel_err(got, ref[r]) < 2e-2, r
     assert torch.isfinite(out).all()
+
+
+def test_layer_host_buffers_match_device_path():
+    """Host inputs stream through the per-block pipeline (copy-in, pooling and
+    builds on a side stream, attention, copy-out); two calls in a row with
+    different inputs must each equal the device-resident forward bit for bit."""
+    from dcc_kv_b200.workloads import layer_inputs
+    nb, L, hq, hkv, d = 4, 1024, 8, 2, 128
+    budgets = {(s, r): [64, 96, 128][(s + 2 * r) % 3] for r in range(nb) for s in range(r)}
+    layer = dk.DccKvSyncLayer(nb, L, hq, hkv, d, budgets, window=256)
+    inputs = [layer_inputs(nb, L, hq, hkv, d, device="cpu", first_seed=s) for s in (11, 23)]
+    want = []
+    for q, k, v in inputs:
+        want.append(layer(q.to(dev()), k.to(dev()), v.to(dev())).cpu())
+    outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for q, _, _ in inputs]
+    pinned = [tuple(t.pin_memory() for t in x) for x in inputs]
+    for (q, k, v), o in zip(pinned, outs):
+        layer(q, k, v, out=o)
+    torch.cuda.synchronize()
+    assert_no_device_timeouts()
+    for o, w in zip(outs, want):
+        assert torch.equal(o, w)
+    with pytest.raises(ValueError):
+        layer(pinned[0][0][:, :4], pinned[0][1], pinned[0][2])
