@@ -57,6 +57,36 @@ def causal_attention_flops():
     return local, compact
 
 
+def attention_bytes(blocks_compact_rows):
+    """Algorithmic HBM bytes of one attention launch over the given blocks:
+    (read, write).  Per block: Q, local K and V read once, its compact K, V
+    (bf16) and bias (fp32) read once, O written once."""
+    read = write = 0
+    for rows in blocks_compact_rows:
+        read += (HQ + 2 * HKV) * BLOCK_LEN * D * 2 + HKV * rows * (2 * D * 2 + 4)
+        write += HQ * BLOCK_LEN * D * 2
+    return read, write
+
+
+# DRAM bytes of one ncu capture of the --profile-attention launch (the last
+# destination block: 16384 causal keys + 7 x 1024 compact keys per KV head):
+# dram__bytes_read.sum / dram__bytes_write.sum.  Its reads are 1.005 x the
+# algorithmic read bytes (no re-reads past L2).  Its writes are lower than the
+# output size because the tail of the output is still in L2 when the launch
+# ends; a full launch writes ~1 GiB, far beyond L2, so its writes are taken
+# at the algorithmic figure.
+PROFILED_DRAM_READ = 231_987_456
+
+
+def attention_traffic():
+    """Estimated DRAM bytes of the full single-GPU attention launch: reads
+    scaled from the profiled block by algorithmic read bytes, writes at the
+    algorithmic output size."""
+    prof_read, _ = attention_bytes([7 * BUDGET])
+    read, write = attention_bytes([r * BUDGET for r in range(N_BLOCKS)])
+    return int(read * PROFILED_DRAM_READ / prof_read + write)
+
+
 class ClockSampler:
     """nvidia-smi clocks and throttle reasons sampled during the timed region."""
 
@@ -231,7 +261,8 @@ def run_gpu(args):
     if ws == 1:
         q, k, v = layer_inputs(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, device="cuda")
         layer = dk.DccKvSyncLayer(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, device=dev)
-        parallelism = "single GPU, 8 logical blocks"
+        layer.schedule = args.schedule
+        parallelism = f"single GPU, 8 logical blocks, {args.schedule} schedule"
     else:
         from dcc_kv_b200.dist_layer import DistributedDccKvLayer
         blocks = [b for b in range(N_BLOCKS) if b % ws == rank]
@@ -245,8 +276,7 @@ def run_gpu(args):
         layer(q, k, v)
     _barrier(ws)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
-    attn_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-               for _ in range(args.steps)]
+    attn_ev = [[] for _ in range(args.steps)]  # (start, end) around each attention launch
     layer.timing_events = attn_ev
     with ClockSampler(dev.index) as clk:
         _barrier(ws)
@@ -258,7 +288,8 @@ def run_gpu(args):
         _barrier(ws)
     layer.timing_events = None
     ms = _max_over_ranks(sum(a.elapsed_time(b) for a, b in ev) / args.steps, ws)
-    a_ms = sum(a.elapsed_time(b) for a, b in attn_ev) / args.steps
+    a_ms = sum(a.elapsed_time(b) for step in attn_ev for a, b in step) / args.steps
+    a_launches = len(attn_ev[0])
     clocks = clk.summary()
     # end to end through the public layer call: pinned host inputs in, output
     # back to host; the single-GPU layer pipelines the copies per block
@@ -299,9 +330,10 @@ def run_gpu(args):
     hbm, tf_burst, tf_sust, src = peaks()
     n_local = q.shape[0]
     if ws == 1:
-        # one launch: every block's causal local segment plus its compact segment
+        # every block's causal local segment plus its compact segment
         kflops = sum(causal_attention_flops())
-        kname = "attention: causal local + compact with logit bias, all 8 blocks, one launch"
+        kname = (f"attention: causal local + compact with logit bias, all 8 blocks, {a_launches} launch(es) "
+                 "per step (flops-weighted)")
     else:
         kflops = n_local * HQ * (BLOCK_LEN * (BLOCK_LEN + 1) // 2) * 4 * D
         kname = f"local causal attention ({n_local} block(s) per GPU, one launch, rank 0)"
@@ -316,7 +348,14 @@ def run_gpu(args):
         "gpu_launches": launches,
         "roofline": {"kernel": kname, "bound": "tensor", "achieved": achieved, "peak": tf_sust,
                      "unit": "TFLOP/s", "frac": achieved / tf_sust, "peak_source": f"{src} bf16 sustained",
-                     "traffic": None, "algorithmic_flops": kflops, "ms_per_launch": a_ms},
+                     "traffic": attention_traffic() / a_launches if ws == 1 else None,
+                     "traffic_source": "ncu DRAM bytes of one block (--profile-attention), reads scaled to "
+                                       "8 blocks by algorithmic read bytes, writes = output size; "
+                                       "averaged over the step's launches",
+                     "algorithmic_bytes": sum(attention_bytes([r * BUDGET for r in range(N_BLOCKS)])) / a_launches
+                     if ws == 1 else None,
+                     "algorithmic_flops": kflops, "launches": a_launches,
+                     "ms_per_launch": a_ms / max(a_launches, 1), "ms_per_step": a_ms},
         "clocks": clocks,
     }
     if args.cpu_baseline and ws == 1:
@@ -364,6 +403,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
+    ap.add_argument("--schedule", choices=("pipelined", "batched"), default="pipelined",
+                    help="single-GPU layer schedule: builds overlapped with per-block attention, or in order")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run two attention launches of one block (small case for ncu) and exit")
     args = ap.parse_args()

@@ -32,6 +32,21 @@ __device__ __forceinline__ int cal_bp(const BuildDesc<Acc>& p) {
   return (int)((int64_t)p.budget < p.L_s ? (int64_t)p.budget : p.L_s);
 }
 
+// sum_t base[t * stride] for t < n, accumulated in t order (the result does
+// not depend on timing), with eight loads in flight per step.
+template <typename S>
+__device__ __forceinline__ double ordered_sum(const S* base, int64_t stride, int n) {
+  double s = 0.0;
+  for (int t0 = 0; t0 < n; t0 += 8) {
+    double v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = t0 + q < n ? (double)base[(int64_t)(t0 + q) * stride] : 0.0;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s += v[q];
+  }
+  return s;
+}
+
 // 64 x 64 partial Gram of a [64][kLdG] shared tile: out[a][a2] = sum_b Z[a][b] Z[a2][b]
 // (thread owns rows ta + 16 i and columns tb + 16 j, i, j < 4; 256 threads).
 __device__ __forceinline__ void tile_gram(const double* zs, double* out) {
@@ -133,6 +148,8 @@ __global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__
   double* tv = gsm + 64 * kLdG;                        // [64]
   double* vv = tv + 64;                                // [64]
   double* res = vv + 64;                               // [64]
+  double* diag = res + 64;                             // [64]
+  double* colbuf = diag + 64;                          // [128]
   // block mass: given, or the pass-2 chunk sums in chunk order
   for (int a = threadIdx.x; a < 64; a += blockDim.x) {
     double s = 0.0;
@@ -140,7 +157,7 @@ __global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__
       if (p.in_mass)
         s = load_side<TIn>(p.in_mass, a);
       else
-        for (int c = 0; c < p.n_chunks; ++c) s += (double)p.massp[(int64_t)c * M + a];
+        s = ordered_sum(p.massp + a, M, p.n_chunks);
     }
     tv[a] = s;
     if (a < M && p.out_mass) p.out_mass[a] = s;
@@ -154,32 +171,41 @@ __global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__
   if (M < Bp) {
     for (int e = threadIdx.x; e < M * M; e += blockDim.x) {
       const int a = e / M, a2 = e % M;
-      double s = 0.0;
-      for (int t = 0; t < p.n_btiles; ++t) s += p.gpart[(int64_t)t * 4096 + a * 64 + a2];
+      const double s = ordered_sum(p.gpart + a * 64 + a2, 4096, p.n_btiles);
       gram[a * kLdG + a2] = s + (a == a2 ? lb : 0.0);
     }
     __syncthreads();
-    chol_inplace(gram, kLdG, M);
-    if (threadIdx.x < 64) vv[threadIdx.x] = tv[threadIdx.x];
+    chol64(gram, kLdG, M, diag, colbuf);
+    if (threadIdx.x < 64) vv[threadIdx.x] = tv[threadIdx.x];  // zero past M
     __syncthreads();
-    chol_solve_parallel(gram, kLdG, M, vv, 1, 1);
+    if (threadIdx.x < 32) chol64_solve_vec(gram, kLdG, diag, M, vv);
+    __syncthreads();
     for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) {
       double w = 0.0;
-      for (int a = 0; a < M; ++a) w = fma(p.G[(int64_t)a * Bp + bb], vv[a], w);
+      for (int a0 = 0; a0 < M; a0 += 8) {
+        double g[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) g[q] = a0 + q < M ? p.G[(int64_t)(a0 + q) * Bp + bb] : 0.0;
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          if (a0 + q < M) w = fma(g[q], vv[a0 + q], w);
+      }
       p.wv[bb] = w > 0.0 ? w : 0.0;
     }
   } else {
     for (int e = threadIdx.x; e < M * Bp; e += blockDim.x) gsm[(e / Bp) * kLdG + e % Bp] = p.G[e];
     __syncthreads();
     gram_cols(gsm, M, Bp, lb, gram);
-    for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) {
+    for (int bb = threadIdx.x; bb < 64; bb += blockDim.x) {
       double s = 0.0;
-      for (int a = 0; a < M; ++a) s = fma(gsm[a * kLdG + bb], tv[a], s);
+      if (bb < Bp)
+        for (int a = 0; a < M; ++a) s = fma(gsm[a * kLdG + bb], tv[a], s);
       vv[bb] = s;
     }
     __syncthreads();
-    chol_inplace(gram, kLdG, Bp);
-    chol_solve_parallel(gram, kLdG, Bp, vv, 1, 1);
+    chol64(gram, kLdG, Bp, diag, colbuf);
+    if (threadIdx.x < 32) chol64_solve_vec(gram, kLdG, diag, Bp, vv);
+    __syncthreads();
     if (threadIdx.x < Bp) vv[threadIdx.x] = fmax(vv[threadIdx.x], 0.0);
     __syncthreads();
     for (int it = 0; it < 100; ++it) {
@@ -210,14 +236,15 @@ __global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__
   }
 }
 
-// ---- 3. X = softmax_b(logits + beta / M), one warp per row ------------------------------
+// ---- 3. X = softmax_b(logits + beta / M), one warp per row, 8 rows per CTA --------------
 template <typename Acc>
 __global__ void __launch_bounds__(256) calib_x_kernel(const __grid_constant__ BuildBatch<Acc> b) {
-  const BuildDesc<Acc>& p = b.p[blockIdx.x];
+  const BuildDesc<Acc>& p = b.p[blockIdx.y];
   if (!(p.stages & kStageValues)) return;
   const int Bp = cal_bp(p), M = p.M;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int a = warp; a < M; a += blockDim.x >> 5) {
+  const int a = blockIdx.x * 8 + warp;
+  if (a < M) {
     double* xr = p.X + (int64_t)a * Bp;
     double mx = -INFINITY;
     for (int bb = lane; bb < Bp; bb += 32) {
@@ -266,24 +293,22 @@ __global__ void __launch_bounds__(256) calib_w_kernel(const __grid_constant__ Bu
   double* gsm = gram + 64 * kLdG;                      // [64][65]
   double* ws = gsm + 64 * kLdG;                        // [64][dv+1]
   const int ldw = dv + 1;
+  double* diag = ws + 64 * ldw;                        // [64]
+  double* colbuf = diag + 64;                          // [128]
   for (int e = threadIdx.x; e < M * dv; e += blockDim.x) {  // Y, chunk order
-    double s = 0.0;
-    for (int c = 0; c < p.n_chunks; ++c) s += (double)p.yp[(int64_t)c * M * dv + e];
+    const double s = ordered_sum(p.yp + e, (int64_t)M * dv, p.n_chunks);
     p.Y[e] = s;
     ws[(e / dv) * ldw + e % dv] = s;
   }
   const double lv = prm.lambda_value;
+  // system size: M x M (push-through form) or B' x B' (literal form)
+  const int n = M < Bp ? M : Bp;
   if (M < Bp) {
     for (int e = threadIdx.x; e < M * M; e += blockDim.x) {
       const int a = e / M, a2 = e % M;
-      double s = 0.0;
-      for (int t = 0; t < p.n_btiles; ++t) s += p.xpart[(int64_t)t * 4096 + a * 64 + a2];
+      const double s = ordered_sum(p.xpart + a * 64 + a2, 4096, p.n_btiles);
       gram[a * kLdG + a2] = s + (a == a2 ? lv : 0.0);
     }
-    __syncthreads();
-    chol_inplace(gram, kLdG, M);
-    chol_solve_parallel(gram, kLdG, M, ws, ldw, dv);
-    for (int e = threadIdx.x; e < M * dv; e += blockDim.x) p.W[e] = ws[(e / dv) * ldw + e % dv];
   } else {
     __syncthreads();
     for (int e = threadIdx.x; e < M * Bp; e += blockDim.x) gsm[(e / Bp) * kLdG + e % Bp] = p.X[e];
@@ -297,9 +322,13 @@ __global__ void __launch_bounds__(256) calib_w_kernel(const __grid_constant__ Bu
       for (int a = 0; a < M; ++a) s = fma(gsm[a * kLdG + bb], p.Y[(int64_t)a * dv + c], s);
       ws[bb * ldw + c] = s;
     }
-    __syncthreads();
-    chol_inplace(gram, kLdG, Bp);
-    chol_solve_parallel(gram, kLdG, Bp, ws, ldw, dv);
+  }
+  __syncthreads();
+  chol64(gram, kLdG, n, diag, colbuf);
+  chol64_solve(gram, kLdG, diag, n, ws, ldw, dv);
+  if (M < Bp) {
+    for (int e = threadIdx.x; e < M * dv; e += blockDim.x) p.W[e] = ws[(e / dv) * ldw + e % dv];
+  } else {
     TIn* outv = static_cast<TIn*>(p.out_values);
     for (int e = threadIdx.x; e < Bp * dv; e += blockDim.x) outv[e] = from_f64<TIn>(ws[(e / dv) * ldw + e % dv]);
   }
@@ -369,9 +398,9 @@ int launch_calibrate(const BuildBatch<Acc>& b, const BuildParams& prm, cudaStrea
   int tmax = 1;
   for (int i = 0; i < b.n; ++i) tmax = b.p[i].n_btiles > tmax ? b.p[i].n_btiles : tmax;
   const size_t smem1 = align_up(2 * 64 * (size_t)(prm.d + 1) * sizeof(ST), 16) + 64 * kLdG * sizeof(double);
-  const size_t smem5 = (2 * 64 * kLdG + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
+  const size_t smem5 = (2 * 64 * kLdG + 64 * (size_t)(prm.dv + 1) + 3 * 64) * sizeof(double);
   const size_t smem6 = (64 * kLdG + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
-  const size_t smem2 = (2 * 64 * kLdG + 3 * 64) * sizeof(double);
+  const size_t smem2 = (2 * 64 * kLdG + 6 * 64) * sizeof(double);
   auto k1 = calib_logits_kernel<TIn, Acc>;
   auto k2 = calib_beta_kernel<TIn, Acc>;
   auto k5 = calib_w_kernel<TIn, Acc>;
@@ -385,7 +414,7 @@ int launch_calibrate(const BuildBatch<Acc>& b, const BuildParams& prm, cudaStrea
   DCC_CHECK(check_launch("calib_logits"));
   k2<<<b.n, 256, smem2, st>>>(b, prm);
   DCC_CHECK(check_launch("calib_beta"));
-  calib_x_kernel<Acc><<<b.n, 256, 0, st>>>(b);
+  calib_x_kernel<Acc><<<dim3(kMaxRepr / 8, b.n), 256, 0, st>>>(b);
   DCC_CHECK(check_launch("calib_x"));
   calib_xgram_kernel<Acc><<<tiles, 256, 0, st>>>(b);
   DCC_CHECK(check_launch("calib_xgram"));

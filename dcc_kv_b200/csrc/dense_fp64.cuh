@@ -122,4 +122,120 @@ __device__ __forceinline__ void chol_solve_parallel(const double* L, int lda, in
   }
 }
 
+// ---- register-resident factor and solves for n <= 64 (the build's hot path) ----
+
+__device__ __forceinline__ void bar_sync_64() { asm volatile("bar.sync 2, 64;\n" ::: "memory"); }
+
+// Cholesky of the leading n x n block (n <= 64) of the SPD matrix A (lower
+// triangle), in place: A = L L^T, zeros written above the diagonal of the
+// n x n block, 1 / L_ii to inv_diag[i].  The block's first 64 threads each
+// hold one row in registers as a window that shifts left by one column per
+// step (r[m] = A_i,k+m at step k), so every register index is static while
+// the step loop stays rolled (straight-line code of this size would be
+// instruction-fetch-bound: it runs once per CTA).  Step k publishes column k
+// through colbuf (2 x 64 doubles, alternating), takes one 64-thread barrier,
+// stores L_ik and applies A_ij -= A_ik A_jk / A_kk for k < j <= i.  Every
+// thread of the block calls it (it ends with __syncthreads()).
+__device__ __forceinline__ void chol64(double* A, int lda, int n, double* inv_diag, double* colbuf) {
+  const int i = threadIdx.x;
+  if (i < 64) {
+    double r[64];
+#pragma unroll
+    for (int m = 0; m < 64; ++m) r[m] = (i < n && m <= i) ? A[i * lda + m] : 0.0;
+    for (int k = 0; k < n; ++k) {
+      double* col = colbuf + (k & 1) * 64;
+      col[i] = r[0];
+      bar_sync_64();
+      const double d = col[k];
+      const double sd = sqrt(d);
+      const bool below = i > k && i < n;
+      if (i == k) {
+        A[i * lda + k] = sd;
+        inv_diag[k] = 1.0 / sd;
+      } else if (below) {
+        A[i * lda + k] = r[0] / sd;
+      }
+      const double t = below ? r[0] / d : 0.0;
+      const int span = below ? i - k : 0;  // columns k+1 .. i are updated
+      // branch-free: every lane loads (clamped index, a broadcast) and
+      // computes; the select keeps rows that are not updated unchanged
+#pragma unroll
+      for (int m = 1; m < 64; ++m) {
+        const double cj = col[min(k + m, 63)];
+        const double u = fma(-t, cj, r[m]);
+        r[m - 1] = m <= span ? u : r[m];
+      }
+      r[63] = 0.0;
+    }
+    if (i < n)
+      for (int j = i + 1; j < n; ++j) A[i * lda + j] = 0.0;
+  }
+  __syncthreads();
+}
+
+// Solve (L L^T) X = B in place for ncols <= blockDim.x right-hand sides, L
+// from chol64 (any n <= 64): column c of B at X[i * ldx + c], rows i < n.
+// One thread per column, substitution through shared memory with four
+// independent partial sums per row; L is read as warp-wide broadcasts.
+__device__ __forceinline__ void chol64_solve(const double* L, int lda, const double* inv_diag, int n, double* X,
+                                             int ldx, int ncols) {
+  const int c = threadIdx.x;
+  if (c < ncols) {
+    double* x = X + c;
+    for (int i = 0; i < n; ++i) {
+      const double* Li = L + i * lda;
+      double s0 = x[i * ldx], s1 = 0.0, s2 = 0.0, s3 = 0.0;
+      int j = 0;
+      for (; j + 4 <= i; j += 4) {
+        s0 = fma(-Li[j], x[j * ldx], s0);
+        s1 = fma(-Li[j + 1], x[(j + 1) * ldx], s1);
+        s2 = fma(-Li[j + 2], x[(j + 2) * ldx], s2);
+        s3 = fma(-Li[j + 3], x[(j + 3) * ldx], s3);
+      }
+      for (; j < i; ++j) s0 = fma(-Li[j], x[j * ldx], s0);
+      x[i * ldx] = ((s0 + s1) + (s2 + s3)) * inv_diag[i];
+    }
+    for (int i = n - 1; i >= 0; --i) {
+      double s0 = x[i * ldx], s1 = 0.0, s2 = 0.0, s3 = 0.0;
+      int j = i + 1;
+      for (; j + 4 <= n; j += 4) {
+        s0 = fma(-L[j * lda + i], x[j * ldx], s0);
+        s1 = fma(-L[(j + 1) * lda + i], x[(j + 1) * ldx], s1);
+        s2 = fma(-L[(j + 2) * lda + i], x[(j + 2) * ldx], s2);
+        s3 = fma(-L[(j + 3) * lda + i], x[(j + 3) * ldx], s3);
+      }
+      for (; j < n; ++j) s0 = fma(-L[j * lda + i], x[j * ldx], s0);
+      x[i * ldx] = ((s0 + s1) + (s2 + s3)) * inv_diag[i];
+    }
+  }
+  __syncthreads();
+}
+
+// Solve (L L^T) v = v in place for one right-hand side v[n] in shared
+// memory, L from chol64 (n <= 64).  One warp: lane l holds rows l and
+// l + 32; each column step broadcasts the solved entry by shuffle.  Called
+// by the 32 threads of one warp only.
+__device__ __forceinline__ void chol64_solve_vec(const double* L, int lda, const double* inv_diag, int n,
+                                                 double* v) {
+  const int l = threadIdx.x & 31;
+  double x0 = l < n ? v[l] : 0.0, x1 = l + 32 < n ? v[l + 32] : 0.0;
+  // branch-free column steps: loads use clamped indices, selects apply them
+  const int r0 = min(l, n - 1), r1 = min(l + 32, n - 1);
+  for (int i = 0; i < n; ++i) {  // forward: L y = v, column by column
+    const double xi = __shfl_sync(0xffffffffu, i < 32 ? x0 : x1, i & 31) * inv_diag[i];
+    const double u0 = fma(-L[r0 * lda + i], xi, x0), u1 = fma(-L[r1 * lda + i], xi, x1);
+    x0 = l == i ? xi : (l > i && l < n ? u0 : x0);
+    x1 = l + 32 == i ? xi : (l + 32 > i && l + 32 < n ? u1 : x1);
+  }
+  for (int i = n - 1; i >= 0; --i) {  // backward: L^T x = y
+    const double xi = __shfl_sync(0xffffffffu, i < 32 ? x0 : x1, i & 31) * inv_diag[i];
+    const double u0 = fma(-L[i * lda + r0], xi, x0), u1 = fma(-L[i * lda + r1], xi, x1);
+    x0 = l == i ? xi : (l < i ? u0 : x0);
+    x1 = l + 32 == i ? xi : (l + 32 < i ? u1 : x1);
+  }
+  if (l < n) v[l] = x0;
+  if (l + 32 < n) v[l + 32] = x1;
+  __syncwarp();
+}
+
 }  // namespace dcc

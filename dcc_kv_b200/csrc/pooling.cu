@@ -7,9 +7,10 @@
 //
 // FPS runs as one thread-block cluster per query set.  Each thread holds one
 // projected point (DPP doubles) in registers for all M steps, so a step is a
-// register dot product, a warp/CTA argmax, one cluster barrier and a DSMEM
-// read of the winner's coordinates -- no N x N matrix, no HBM traffic.  The
-// argmax breaks ties toward the lower index, as torch.argmax does.
+// register dot product, a warp/CTA argmax, DSMEM stores of each CTA's winner
+// into every CTA of the cluster and one cluster barrier -- no N x N matrix,
+// no HBM traffic.  The argmax breaks ties toward the lower index, as
+// torch.argmax does.
 #include <cooperative_groups.h>
 
 #include <type_traits>
@@ -50,41 +51,80 @@ __device__ __forceinline__ int64_t set_row_offset(const SetDesc& s, int64_t i) {
 
 // ---- projection: normed[i] = n(n(Q_i P^T)),  n(z) = z / (||z|| + 1e-8) ------
 // One thread per query row holds all DPP projected coordinates in registers.
-// P[k][c] = +-mag, so z_k = sum_c +-(q_c * mag): q_c * mag is exact in FP64
+// P[k][c] = +-mag sits in shared memory as FP64 (zero for k >= d_p), so
+// z_k = sum_c fma(P[k][c], q_c, .): the product +-mag * q_c is exact in FP64
 // for bf16 / fp32 queries (as in the reference's FP64 matmul), only the
-// summation order differs.  Column c's signs sit in one 64-bit word.
+// summation order differs.
 template <typename T>
 __device__ __forceinline__ double load_row_elem(const T* q, int c) { return to_f64<T>(q[c]); }
+
+// Eight consecutive elements from a 16-byte-aligned address, widened to FP64.
+template <typename T>
+__device__ __forceinline__ void load8(const T* p, double* out);
+template <>
+__device__ __forceinline__ void load8<__nv_bfloat16>(const __nv_bfloat16* p, double* out) {
+  const uint4 v = *reinterpret_cast<const uint4*>(p);
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    out[2 * i] = (double)__uint_as_float(w[i] << 16);
+    out[2 * i + 1] = (double)__uint_as_float(w[i] & 0xffff0000u);
+  }
+}
+template <>
+__device__ __forceinline__ void load8<float>(const float* p, double* out) {
+  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
+  out[0] = a.x; out[1] = a.y; out[2] = a.z; out[3] = a.w;
+  out[4] = b.x; out[5] = b.y; out[6] = b.z; out[7] = b.w;
+}
+template <>
+__device__ __forceinline__ void load8<double>(const double* p, double* out) {
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const double2 v = reinterpret_cast<const double2*>(p)[i];
+    out[2 * i] = v.x;
+    out[2 * i + 1] = v.y;
+  }
+}
+
+template <int DPP>
+__device__ __forceinline__ void project_accumulate(double* z, const double* pm_c, double qc) {
+#pragma unroll
+  for (int k = 0; k < DPP; k += 2) {
+    const double2 pv = *reinterpret_cast<const double2*>(pm_c + k);
+    z[k] = fma(pv.x, qc, z[k]);
+    z[k + 1] = fma(pv.y, qc, z[k + 1]);
+  }
+}
 
 template <typename T, int DPP>
 __global__ void __launch_bounds__(128) project_kernel(const __grid_constant__ SetBatch b,
                                                       const __grid_constant__ ProjBits proj, int d,
                                                       int dp) {
-  __shared__ unsigned long long colsign[256];
+  extern __shared__ __align__(16) double pm[];  // [d][DPP]
   const SetDesc& s = b.p[blockIdx.y];
-  for (int c = threadIdx.x; c < d; c += blockDim.x) {
-    unsigned long long w = 0;
-    for (int k = 0; k < dp; ++k) {
-      const int bit = k * d + c;
-      if ((proj.bits[bit >> 5] >> (bit & 31)) & 1u) w |= 1ull << k;
-    }
-    colsign[c] = w;
+  const double mag = (double)proj.mag;
+  for (int e = threadIdx.x; e < d * DPP; e += blockDim.x) {
+    const int c = e / DPP, k = e - c * DPP;
+    const int bit = k * d + c;
+    pm[e] = k < dp ? (((proj.bits[bit >> 5] >> (bit & 31)) & 1u) ? mag : -mag) : 0.0;
   }
   __syncthreads();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= s.n) return;
   const T* q = static_cast<const T*>(s.q) + set_row_offset(s, i);
-  const double mag = (double)proj.mag;
   double z[DPP];
 #pragma unroll
   for (int k = 0; k < DPP; ++k) z[k] = 0.0;
-  for (int c = 0; c < d; ++c) {
-    const double qp = load_row_elem<T>(q, c) * mag;
-    const unsigned long long w = colsign[c];
+  if (d % 8 == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
+    for (int c0 = 0; c0 < d; c0 += 8) {
+      double qv[8];
+      load8<T>(q + c0, qv);
 #pragma unroll
-    for (int k = 0; k < DPP; ++k) {
-      if (k < dp) z[k] += ((w >> k) & 1ull) ? qp : -qp;
+      for (int j = 0; j < 8; ++j) project_accumulate<DPP>(z, pm + (c0 + j) * DPP, qv[j]);
     }
+  } else {
+    for (int c = 0; c < d; ++c) project_accumulate<DPP>(z, pm + c * DPP, load_row_elem<T>(q, c));
   }
   double ss = 0.0;
 #pragma unroll
@@ -99,6 +139,24 @@ __global__ void __launch_bounds__(128) project_kernel(const __grid_constant__ Se
   inv = 1.0 / (sqrt(ss) + 1e-8);  // normalised again inside FPS, :63
 #pragma unroll
   for (int k = 0; k < DPP; ++k) s.normed[i * DPP + k] = z[k] * inv;
+}
+
+// Argmax keys: a double maps to a uint64 that orders like the double (larger
+// key = larger value; -0 is folded into +0 first so that equal values get
+// equal keys), and ties go to the lower index, as torch.argmax does.
+__device__ __forceinline__ unsigned long long order_key(double v) {
+  const long long b = __double_as_longlong(v + 0.0);
+  return b >= 0 ? (unsigned long long)b | 0x8000000000000000ull : ~(unsigned long long)b;
+}
+// Warp-wide argmax of (key, idx) with three redux instructions; every lane
+// returns the winning key and index.
+__device__ __forceinline__ void warp_argmax_key(unsigned long long& key, int& idx, unsigned mask = 0xffffffffu) {
+  const unsigned hi = __reduce_max_sync(mask, (unsigned)(key >> 32));
+  const bool m1 = (unsigned)(key >> 32) == hi;
+  const unsigned lo = __reduce_max_sync(mask, m1 ? (unsigned)key : 0u);
+  const bool m2 = m1 && (unsigned)key == lo;
+  idx = (int)__reduce_min_sync(mask, m2 ? (unsigned)idx : 0x7fffffffu);
+  key = ((unsigned long long)hi << 32) | lo;
 }
 
 struct Cand {
@@ -119,13 +177,20 @@ __device__ __forceinline__ void warp_argmax(double& v, int& i) {
 
 template <int DPP>
 struct ClusterSlot {
-  double v;
+  unsigned long long key;
   int i;
   int pad;
   double coords[DPP];
 };
 
 // ---- FPS, register-resident: one cluster of CL CTAs x T threads per set -------
+// A step: warp argmax (redux) -> per-warp winners in shared memory -> warp 0
+// takes the CTA winner and stores it (key, index, coordinates) into slot
+// [step parity][own rank] of every CTA of the cluster -> one cluster barrier
+// -> every warp reduces the cluster's slots from its own shared memory and
+// reads the winner's coordinates there.  Slots are double-buffered by step
+// parity: a CTA overwrites a parity only after the next barrier, which every
+// CTA reaches after its reads of that parity.
 template <typename T, int DPP, int TPB>
 __global__ void __launch_bounds__(TPB) fps_cluster_kernel(const __grid_constant__ SetBatch b, int M,
                                                           int d) {
@@ -134,10 +199,11 @@ __global__ void __launch_bounds__(TPB) fps_cluster_kernel(const __grid_constant_
   const int rank = (int)cluster.block_rank();
   const SetDesc& s = b.p[blockIdx.x / cl];
   constexpr int NW = TPB / 32;
-  __shared__ Cand wbest[NW];
+  __shared__ unsigned long long wkey[NW];
+  __shared__ int widx[NW];
   __shared__ double wcoords[NW][DPP];
-  __shared__ ClusterSlot<DPP> cslot[2];
-  __shared__ double ynew[DPP];
+  __shared__ ClusterSlot<DPP> cslot[2][16];
+  __shared__ double ystart[DPP];
   __shared__ int sel[256];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int me = rank * TPB + threadIdx.x;
@@ -145,72 +211,61 @@ __global__ void __launch_bounds__(TPB) fps_cluster_kernel(const __grid_constant_
   double x[DPP];
 #pragma unroll
   for (int k = 0; k < DPP; ++k) x[k] = valid ? s.normed[(int64_t)me * DPP + k] : 0.0;
-  if (threadIdx.x < DPP) ynew[threadIdx.x] = s.normed[s.start * DPP + threadIdx.x];
+  if (threadIdx.x < DPP) ystart[threadIdx.x] = s.normed[s.start * DPP + threadIdx.x];
   if (threadIdx.x == 0) sel[0] = (int)s.start;
   __syncthreads();
   double mind;
   {
-    double dot = 0.0;
+    double dp4[4] = {0.0, 0.0, 0.0, 0.0};
 #pragma unroll
-    for (int k = 0; k < DPP; ++k) dot = fma(x[k], ynew[k], dot);
-    mind = valid ? 1.0 - dot : -INFINITY;
+    for (int k = 0; k < DPP; ++k) dp4[k & 3] = fma(x[k], ystart[k], dp4[k & 3]);
+    mind = valid ? 1.0 - ((dp4[0] + dp4[1]) + (dp4[2] + dp4[3])) : -INFINITY;
   }
   for (int t = 1; t < M; ++t) {
     const int par = t & 1;
-    double v = mind;
-    int i = valid ? me : 0x7fffffff;
-    warp_argmax(v, i);
-    if (valid && i == me) {
+    unsigned long long key = order_key(mind);
+    int bi = valid ? me : 0x7fffffff;
+    warp_argmax_key(key, bi);
+    if (valid && bi == me) {
 #pragma unroll
       for (int k = 0; k < DPP; ++k) wcoords[warp][k] = x[k];
     }
-    if (lane == 0) wbest[warp] = Cand{v, i};
+    if (lane == 0) {
+      wkey[warp] = key;
+      widx[warp] = bi;
+    }
     __syncthreads();
     if (warp == 0) {
-      double bv = lane < NW ? wbest[lane].v : -INFINITY;
-      int bi = lane < NW ? wbest[lane].i : 0x7fffffff;
-      int bw = lane < NW ? lane : 0;
-      // reduce carrying the owning warp
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const double v2 = __shfl_xor_sync(0xffffffffu, bv, o);
-        const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
-        const int w2 = __shfl_xor_sync(0xffffffffu, bw, o);
-        if (better(v2, i2, bv, bi)) { bv = v2; bi = i2; bw = w2; }
+      unsigned long long ck = lane < NW ? wkey[lane] : 0ull;
+      int ci = lane < NW ? widx[lane] : 0x7fffffff;
+      const int my_i = ci;
+      warp_argmax_key(ck, ci);
+      const int bw = __ffs(__ballot_sync(0xffffffffu, lane < NW && my_i == ci)) - 1;
+      for (int dst = 0; dst < cl; ++dst) {
+        ClusterSlot<DPP>* rs = cluster.map_shared_rank(&cslot[par][rank], dst);
+        if (lane < DPP) rs->coords[lane] = wcoords[bw][lane];
+        if (DPP > 32 && lane + 32 < DPP) rs->coords[lane + 32] = wcoords[bw][lane + 32];
+        if (lane == 0) {
+          rs->key = ck;
+          rs->i = ci;
+        }
       }
-      if (lane < DPP) cslot[par].coords[lane] = wcoords[bw][lane];
-      if (DPP > 32 && lane + 32 < DPP) cslot[par].coords[lane + 32] = wcoords[bw][lane + 32];
-      if (lane == 0) { cslot[par].v = bv; cslot[par].i = bi; }
     }
     if (cl > 1) cluster.sync(); else __syncthreads();
-    if (warp == 0) {
-      double gv = -INFINITY;
-      int gi = 0x7fffffff, gr = 0;  // lanes >= cl carry an empty candidate from rank 0
-      if (lane < cl) {
-        ClusterSlot<DPP>* rs = cluster.map_shared_rank(&cslot[par], lane);
-        gv = rs->v;
-        gi = rs->i;
-        gr = lane;
-      }
+    unsigned long long gk = lane < cl ? cslot[par][lane].key : 0ull;
+    int gi = lane < cl ? cslot[par][lane].i : 0x7fffffff;
+    const int my_gi = gi;
+    warp_argmax_key(gk, gi);
+    const int gw = __ffs(__ballot_sync(0xffffffffu, lane < cl && my_gi == gi)) - 1;
+    if (threadIdx.x == 0) sel[t] = gi;
+    const double* y = cslot[par][gw].coords;
+    double dp4[4] = {0.0, 0.0, 0.0, 0.0};  // four independent FMA chains
 #pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        const double v2 = __shfl_xor_sync(0xffffffffu, gv, o);
-        const int i2 = __shfl_xor_sync(0xffffffffu, gi, o);
-        const int r2 = __shfl_xor_sync(0xffffffffu, gr, o);
-        if (better(v2, i2, gv, gi)) { gv = v2; gi = i2; gr = r2; }
-      }
-      ClusterSlot<DPP>* ws = cluster.map_shared_rank(&cslot[par], gr);
-      if (lane < DPP) ynew[lane] = ws->coords[lane];
-      if (DPP > 32 && lane + 32 < DPP) ynew[lane + 32] = ws->coords[lane + 32];
-      if (lane == 0) sel[t] = gi;
-    }
-    __syncthreads();
-    double dot = 0.0;
-#pragma unroll
-    for (int k = 0; k < DPP; ++k) dot = fma(x[k], ynew[k], dot);
+    for (int k = 0; k < DPP; ++k) dp4[k & 3] = fma(x[k], y[k], dp4[k & 3]);
+    const double dot = (dp4[0] + dp4[1]) + (dp4[2] + dp4[3]);
     if (valid) mind = fmin(mind, 1.0 - dot);
   }
-  // keep this CTA's shared memory alive until every remote read finished
+  // keep this CTA's shared memory alive until every remote access finished
   if (cl > 1) cluster.sync();
   if (rank == 0) {
     for (int t = threadIdx.x; t < M; t += TPB) s.out_idx[t] = sel[t];
@@ -342,13 +397,19 @@ static int run_pooling(SetBatch& b, int d, int M, int dp, const ProjBits& proj, 
   // projection
   const int blocks_x = (max_n + 127) / 128;
   dim3 grid(blocks_x, b.n);
+  const size_t pm_bytes = (size_t)d * dpp * sizeof(double);
+  auto launch = [&](auto kern) -> int {
+    DCC_CHECK(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pm_bytes),
+                         "project smem"));
+    kern<<<grid, 128, pm_bytes, st>>>(b, proj, d, dp);
+    return check_launch("project");
+  };
   switch (dpp) {
-    case 8: project_kernel<T, 8><<<grid, 128, 0, st>>>(b, proj, d, dp); break;
-    case 16: project_kernel<T, 16><<<grid, 128, 0, st>>>(b, proj, d, dp); break;
-    case 32: project_kernel<T, 32><<<grid, 128, 0, st>>>(b, proj, d, dp); break;
-    default: project_kernel<T, 64><<<grid, 128, 0, st>>>(b, proj, d, dp); break;
+    case 8: DCC_CHECK(launch(project_kernel<T, 8>)); break;
+    case 16: DCC_CHECK(launch(project_kernel<T, 16>)); break;
+    case 32: DCC_CHECK(launch(project_kernel<T, 32>)); break;
+    default: DCC_CHECK(launch(project_kernel<T, 64>)); break;
   }
-  DCC_CHECK(check_launch("project"));
   switch (dpp) {
     case 8: return run_fps<T, 8>(b, M, d, max_n, st);
     case 16: return run_fps<T, 16>(b, M, d, max_n, st);

@@ -62,20 +62,48 @@ __global__ void __launch_bounds__(1024) topk_kernel(const __grid_constant__ Buil
   for (int shift = (int)sizeof(U) * 8 - 8; shift >= 0; shift -= 8) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0;
     __syncthreads();
-    for (int64_t j = threadIdx.x; j < L; j += blockDim.x) {
-      const U k = key_of<U>(u[j]);
-      if ((k & mask) == prefix) atomicAdd(&hist[(unsigned)((k >> shift) & 0xFF)], 1u);
+    // scores of similar magnitude share their leading digits, so lanes that
+    // hit the same bin are merged into one shared-memory atomic
+    const int64_t jend = (L + blockDim.x - 1) / blockDim.x * blockDim.x;
+    for (int64_t j = threadIdx.x; j < jend; j += blockDim.x) {
+      const U k = j < L ? key_of<U>(u[j]) : (U)0;
+      const bool act = j < L && (k & mask) == prefix;
+      const unsigned am = __ballot_sync(0xffffffffu, act);
+      if (act) {
+        const unsigned bin = (unsigned)((k >> shift) & 0xFF);
+        const unsigned peers = __match_any_sync(am, bin);
+        if ((threadIdx.x & 31) == (unsigned)(__ffs(peers) - 1)) atomicAdd(&hist[bin], (unsigned)__popc(peers));
+      }
     }
     __syncthreads();
-    if (threadIdx.x == 0) {
-      int cum = 0, dsel = 0;
-      for (int dgt = 255; dgt >= 0; --dgt) {
-        const int h = (int)hist[dgt];
-        if (cum + h >= need) { dsel = dgt; break; }
-        cum += h;
+    if (threadIdx.x < 32) {
+      // lane l owns digits 255 - 8l .. 248 - 8l; find the digit where the
+      // running count from the top first reaches `need`
+      const int l = threadIdx.x;
+      int h8[8], sum = 0;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        h8[q] = (int)hist[255 - 8 * l - q];
+        sum += h8[q];
       }
-      s_take = need - cum;
-      s_prefix = prefix | ((U)dsel << shift);
+      int incl = sum;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (l >= o) incl += v;
+      }
+      const int before = incl - sum;
+      const bool mine = before < need && need <= incl;
+      if (mine) {
+        int cum = before, dsel = 255 - 8 * l;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          if (cum + h8[q] >= need) { dsel = 255 - 8 * l - q; break; }
+          cum += h8[q];
+        }
+        s_take = need - cum;
+        s_prefix = prefix | ((U)dsel << shift);
+      }
     }
     __syncthreads();
     need = s_take;
@@ -136,9 +164,22 @@ __global__ void __launch_bounds__(1024) topk_kernel(const __grid_constant__ Buil
     }
   }
   for (int i = threadIdx.x; i < B; i += blockDim.x) p.out_idx[i] = ent[i].idx;
-  for (int64_t e = threadIdx.x; e < (int64_t)B * prm.d; e += blockDim.x) {
-    const int64_t r = e / prm.d, c = e - r * prm.d;
-    outk[e] = K[(int64_t)ent[r].idx * p.ld_k + c];
+  // C_K gather: 16-byte chunks when rows allow it
+  const int row_bytes = prm.d * (int)sizeof(TIn);
+  if (row_bytes % 16 == 0 && (p.ld_k * (int64_t)sizeof(TIn)) % 16 == 0 &&
+      (reinterpret_cast<uintptr_t>(K) & 15) == 0 && (reinterpret_cast<uintptr_t>(outk) & 15) == 0) {
+    const int cpr = row_bytes / 16;  // chunks per row
+    for (int64_t e = threadIdx.x; e < (int64_t)B * cpr; e += blockDim.x) {
+      const int64_t r = e / cpr;
+      const int c = (int)(e - r * cpr);
+      const uint4* src = reinterpret_cast<const uint4*>(K + (int64_t)ent[r].idx * p.ld_k) + c;
+      reinterpret_cast<uint4*>(outk + r * prm.d)[c] = *src;
+    }
+  } else {
+    for (int64_t e = threadIdx.x; e < (int64_t)B * prm.d; e += blockDim.x) {
+      const int64_t r = e / prm.d, c = e - r * prm.d;
+      outk[e] = K[(int64_t)ent[r].idx * p.ld_k + c];
+    }
   }
 }
 

@@ -217,8 +217,10 @@ class DistributedDccKvLayer:
                                    input_split_sizes=self.send_splits, group=self.group)
         # local causal attention meanwhile, on the main stream
         scale = 1.0 / math.sqrt(self.d)
-        ev = self.timing_events[self.timing_index] if self.timing_events else None
-        if ev is not None:
+        ev = None
+        if self.timing_events:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            self.timing_events[self.timing_index].append(ev)
             ev[0].record(main)
         run_attention(self.local_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
         if ev is not None:

@@ -88,7 +88,12 @@ class DccKvSyncLayer:
         self._ws = None
         self._host_out = None
         self._staging = None
-        # optional (start, end) CUDA events per step around the local-attention launch
+        self._streams = None
+        # "pipelined": builds on a side stream overlapped with per-block
+        # attention; "batched": pooling, builds, one attention launch, in order
+        self.schedule = "pipelined"
+        # optional per-step lists that collect (start, end) CUDA events around
+        # each attention launch
         self.timing_events = None
         self.timing_index = 0
 
@@ -97,7 +102,7 @@ class DccKvSyncLayer:
         key = (q.data_ptr(), k.data_ptr(), v.data_ptr())
         if self._bound == key:
             return
-        if self._staging is not None:
+        if self._streams is not None:
             # the workspace below may still be in use by the side stream
             torch.cuda.current_stream(self.device).wait_stream(self._streams[1])
         g = self.group
@@ -165,19 +170,95 @@ class DccKvSyncLayer:
             return self._forward_host(q, k, v, out)
         self.check_inputs(q, k, v)
         self._bind(q, k, v)
-        dev = self.device
-        select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
-        run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
-        scale = 1.0 / math.sqrt(self.d)
-        ev = self.timing_events[self.timing_index] if self.timing_events else None
-        if ev is not None:
-            ev[0].record(torch.cuda.current_stream(dev))
-        run_attention(self.attn_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
-        if ev is not None:
-            ev[1].record(torch.cuda.current_stream(dev))
+        if self.schedule == "batched":
+            self._forward_batched()
+        else:
+            self._ensure_streams()
+            self._run_blocks(pool_all=True)
         return self.out
 
     __call__ = forward
+
+    def _attention(self, problems) -> None:
+        dev = self.device
+        main = torch.cuda.current_stream(dev)
+        ev = None
+        if self.timing_events:
+            ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            self.timing_events[self.timing_index].append(ev)
+            ev[0].record(main)
+        run_attention(problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code, dev)
+        if ev is not None:
+            ev[1].record(main)
+
+    def _forward_batched(self) -> None:
+        """Everything on the current stream: all pooling, all builds, then one
+        attention launch over every block."""
+        dev = self.device
+        select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
+        run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
+        self._attention(self.attn_problems)
+
+    def _ensure_streams(self) -> None:
+        if self._streams is None:
+            dev = self.device
+            lo, hi = torch.cuda.Stream.priority_range()
+            # copy-in, builds (high priority: their few CTAs are dispatched ahead
+            # of the attention CTAs that fill the GPU), copy-out
+            self._streams = tuple(torch.cuda.Stream(device=dev, priority=p) for p in (0, hi, 0))
+            self._events = [[torch.cuda.Event() for _ in range(self.nb)] for _ in range(4)]
+            self._compute_done = torch.cuda.Event()
+
+    def _run_blocks(self, pool_all: bool, copy_in=None, copy_out=None) -> None:
+        """Per-block schedule.  Side stream (high priority): pooling, then for
+        b = 1 .. nb-1 the builds s -> b; current stream: attention of block b
+        as soon as its compacts are built (block 0 needs none and starts at
+        once), so the latency-bound pooling / build kernels share the GPU
+        with attention instead of running before it.  ``copy_in(b)`` /
+        ``copy_out(b)``, when given, run on the copy-in / copy-out streams."""
+        dev = self.device
+        h2d, side, d2h = self._streams
+        copied, built, attended, drained = self._events
+        main = torch.cuda.current_stream(dev)
+        if copy_in is not None:
+            # the previous call's kernels must be done reading the staging buffers
+            h2d.wait_event(self._compute_done)
+            with torch.cuda.stream(h2d):
+                for b in range(self.nb):
+                    copy_in(b)
+                    copied[b].record(h2d)
+        side.wait_stream(main)
+        if pool_all:
+            with torch.cuda.stream(side):
+                select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
+        for b in range(self.nb):
+            if b > 0:
+                with torch.cuda.stream(side):
+                    if copy_in is not None:
+                        side.wait_event(copied[b])
+                    if not pool_all:
+                        select_query_sets(self.sets[self.sets_of[b]], self.d, self.M, self.dp, self.seed,
+                                          self.code, dev)
+                    run_build_problems(self.build[self.build_of[b]], self.d, self.d, self.lb, self.lv,
+                                       self.code, dev, self._ws)
+                    built[b].record(side)
+                main.wait_event(built[b])
+            if copy_in is not None:
+                main.wait_event(copied[b])
+            if copy_out is not None:
+                main.wait_event(drained[b])  # the previous call's copy-out of this block
+            self._attention([self.attn_problems[b]])
+            if copy_out is not None:
+                attended[b].record(main)
+                d2h.wait_event(attended[b])
+                with torch.cuda.stream(d2h):
+                    copy_out(b)
+                    drained[b].record(d2h)
+        if self.nb == 1:
+            main.wait_stream(side)
+        self._compute_done.record(main)
+        if copy_out is not None:
+            main.wait_stream(d2h)
 
     def _forward_host(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                       out: Optional[torch.Tensor]) -> torch.Tensor:
@@ -203,57 +284,33 @@ class DccKvSyncLayer:
             self._staging = (torch.empty(exp_q, dtype=self.dtype, device=dev),
                              torch.empty(exp_kv, dtype=self.dtype, device=dev),
                              torch.empty(exp_kv, dtype=self.dtype, device=dev))
-            lo, hi = torch.cuda.Stream.priority_range()
-            self._streams = tuple(torch.cuda.Stream(device=dev, priority=p) for p in (0, hi, 0))
-            self._events = [[torch.cuda.Event() for _ in range(self.nb)] for _ in range(4)]
-            self._compute_done = None
+        self._ensure_streams()
         dq, dk_, dv = self._staging
         self._bind(dq, dk_, dv)
-        h2d, side, d2h = self._streams
-        copied, built, attended, drained = self._events
-        main = torch.cuda.current_stream(dev)
-        # the previous call's kernels must be done reading the staging buffers
-        if self._compute_done is None:
-            self._compute_done = torch.cuda.Event()
-            h2d.wait_stream(main)
-        else:
-            h2d.wait_event(self._compute_done)
-        with torch.cuda.stream(h2d):
-            for b in range(self.nb):
-                dq[b].copy_(q[b], non_blocking=True)
-                dk_[b].copy_(k[b], non_blocking=True)
-                dv[b].copy_(v[b], non_blocking=True)
-                copied[b].record(h2d)
-        scale = 1.0 / math.sqrt(self.d)
-        side.wait_stream(main)
-        for b in range(self.nb):
-            if b > 0:
-                side.wait_event(copied[b])
-                with torch.cuda.stream(side):
-                    select_query_sets(self.sets[self.sets_of[b]], self.d, self.M, self.dp, self.seed, self.code, dev)
-                    run_build_problems(self.build[self.build_of[b]], self.d, self.d, self.lb, self.lv, self.code,
-                                       dev, self._ws)
-                built[b].record(side)
-                main.wait_event(built[b])
-            main.wait_event(copied[b])
-            main.wait_event(drained[b])  # the previous call's copy-out of this block
-            run_attention([self.attn_problems[b]], self.hq, self.hkv, self.d, scale, self.code, dev)
-            attended[b].record(main)
-            d2h.wait_event(attended[b])
-            with torch.cuda.stream(d2h):
-                out[b].copy_(self.out[b], non_blocking=True)
-                drained[b].record(d2h)
-        self._compute_done.record(main)
-        main.wait_stream(d2h)
+
+        def copy_in(b):
+            dq[b].copy_(q[b], non_blocking=True)
+            dk_[b].copy_(k[b], non_blocking=True)
+            dv[b].copy_(v[b], non_blocking=True)
+
+        def copy_out(b):
+            out[b].copy_(self.out[b], non_blocking=True)
+
+        self._run_blocks(pool_all=False, copy_in=copy_in, copy_out=copy_out)
         return out
 
     def launches_per_forward(self) -> int:
-        """Kernel launches one forward enqueues (batch caps of the C library:
-        64 query sets, 96 build edges, 8 tcgen05 attention problems per launch)."""
+        """Kernel launches one device-input forward enqueues (batch caps of
+        the C library: 64 query sets, 128 build edges, 8 tcgen05 attention
+        problems per launch)."""
         sets = len(self.sets)
         pool = 0 if sets == 0 else (2 if self.m_eff < self.group * self.window else 1) * -(-sets // 64)
-        build = build_launch_count(len(self.build), self.code, self.d)
-        attn = -(-len(self.attn_problems) // 8)
+        if self.schedule == "batched":
+            build = build_launch_count(len(self.build), self.code, self.d)
+            attn = -(-len(self.attn_problems) // 8)
+        else:
+            build = sum(build_launch_count(len(self.build[part]), self.code, self.d) for part in self.build_of)
+            attn = len(self.attn_problems)
         return pool + build + attn
 
     def compact(self, s: int, r: int, h: int):

@@ -112,7 +112,12 @@ def test_layer_host_buffers_match_device_path():
     inputs = [layer_inputs(nb, L, hq, hkv, d, device="cpu", first_seed=s) for s in (11, 23)]
     want = []
     for q, k, v in inputs:
-        want.append(layer(q.to(dev()), k.to(dev()), v.to(dev())).cpu())
+        dq, dk_, dv = q.to(dev()), k.to(dev()), v.to(dev())
+        layer.schedule = "batched"
+        want.append(layer(dq, dk_, dv).cpu())
+        # the overlapped per-block schedule runs the same kernels per block
+        layer.schedule = "pipelined"
+        assert torch.equal(layer(dq, dk_, dv).cpu(), want[-1])
     outs = [torch.empty(q.shape, dtype=q.dtype).pin_memory() for q, _, _ in inputs]
     pinned = [tuple(t.pin_memory() for t in x) for x in inputs]
     for (q, k, v), o in zip(pinned, outs):
