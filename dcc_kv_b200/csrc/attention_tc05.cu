@@ -5,11 +5,8 @@
 // every K/V tile is loaded once for 256 rows.  Warp roles (384 threads):
 //   warps 0-3  softmax for head A (thread = query row = TMEM lane)
 //   warps 4-7  softmax for head B
-//   warp  8    TMA producer (Q once; K, V tiles of 128 keys, 2-stage rings;
-//              the per-key bias tile through shared memory).  A K stage is
-//              refilled as soon as both heads' S MMAs of its tile finished, a
-//              V stage (and its bias) once both PV MMAs did, so the next K
-//              tile is already resident when the MMA warp wants S(j+1).
+//   warp  8    TMA producer (Q once; K, V tiles of 128 keys, 2-stage ring;
+//              the per-key bias tile through shared memory)
 //   warp  9    TMEM owner and MMA issuer (one elected thread)
 //   warps 10-11 idle
 // Registers: launched at 168 per thread (3 warps per SM sub-partition), the
@@ -82,7 +79,7 @@ struct Smem {
   unsigned char k[2][kTileBytes];    // stages
   unsigned char v[2][kTileBytes];
   __align__(16) float bias[2][kKeys];
-  uint64_t bar_q, bar_k[2], bar_v[2], bar_bias[2], bar_kfree[2], bar_vfree[2], bar_s[2], bar_p[2], bar_o[2];
+  uint64_t bar_q, bar_k[2], bar_v[2], bar_bias[2], bar_empty[2], bar_s[2], bar_p[2], bar_o[2];
   uint32_t tmem;
 };
 
@@ -145,11 +142,10 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
     tma_load_3d(sm.q[1], &p.q, &sm.bar_q, 0, (int)q0, hB);
     tma_load_3d(sm.q[1] + 16384, &p.q, &sm.bar_q, 64, (int)q0, hB);
   }
-  int k_issued = 0, v_issued = 0;
+  int issued = 0;
   for (int j = 0; j < n_tiles; ++j) {
     const int st = j & 1;
-    // K stage: both S MMAs of tile j - 2 finished
-    if (j >= 2 && !warp_wait(&sm.bar_kfree[st], ((j >> 1) - 1) & 1)) {
+    if (j >= 2 && !warp_wait(&sm.bar_empty[st], ((j >> 1) - 1) & 1)) {
       ok = false;
       break;
     }
@@ -159,15 +155,6 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
       mbar_expect_tx(&sm.bar_k[st], kTileBytes);
       tma_load_3d(sm.k[st], &sg.k, &sm.bar_k[st], 0, (int)t.t0, hk);
       tma_load_3d(sm.k[st] + 16384, &sg.k, &sm.bar_k[st], 64, (int)t.t0, hk);
-    }
-    __syncwarp();
-    k_issued = j + 1;
-    // V stage and bias: both PV MMAs (hence both softmaxes) of tile j - 2 finished
-    if (j >= 2 && !warp_wait(&sm.bar_vfree[st], ((j >> 1) - 1) & 1)) {
-      ok = false;
-      break;
-    }
-    if (lane == 0) {
       mbar_expect_tx(&sm.bar_v[st], kTileBytes);
       tma_load_3d(sm.v[st], &sg.v, &sm.bar_v[st], 0, (int)t.t0, hk);
       tma_load_3d(sm.v[st] + 16384, &sg.v, &sm.bar_v[st], 64, (int)t.t0, hk);
@@ -180,14 +167,15 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
       sm.bias[st][c] = (bg && key < t.kend) ? __ldg(bg + key) * 1.4426950408889634f : 0.f;  // log2 units
     }
     mbar_arrive(&sm.bar_bias[st]);
-    v_issued = j + 1;
+    issued = j + 1;
   }
   if (!ok) atomicOr(&g_attn_error, 1u);
-  // copies still in flight land before the CTA can exit (a K tile may have
-  // been issued without its V tile when the V wait gave up)
+  // copies still in flight land before the CTA can exit
   if (lane == 0) {
-    for (int j = k_issued - 2 < 0 ? 0 : k_issued - 2; j < k_issued; ++j) mbar_wait(&sm.bar_k[j & 1], (j >> 1) & 1);
-    for (int j = v_issued - 2 < 0 ? 0 : v_issued - 2; j < v_issued; ++j) mbar_wait(&sm.bar_v[j & 1], (j >> 1) & 1);
+    for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; ++j) {
+      mbar_wait(&sm.bar_k[j & 1], (j >> 1) & 1);
+      mbar_wait(&sm.bar_v[j & 1], (j >> 1) & 1);
+    }
     mbar_wait(&sm.bar_q, 0);
   }
 }
@@ -196,7 +184,6 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
 // Issue order per tile j:  PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)  (S_A(0), S_B(0) first),
 // so head A's next scores are ready while head B's softmax still runs.  S(j+1)
 // overwrites P(j) in TMEM only after PV(j), issued earlier from this thread.
-// K stage t is released (bar_kfree) after S_B(t), V stage t (bar_vfree) after PV_B(t).
 __device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int lane) {
   const uint32_t id_s = idesc_bf16_f32(128, 128, 0, 0);
   const uint32_t id_pv = idesc_bf16_f32(128, 128, 0, 1);
@@ -227,8 +214,6 @@ __device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int
       tc_fence_after();
       issue_s(0, 0);
       issue_s(1, 0);
-      if (lane == 0) umma_commit(&sm.bar_kfree[0]);
-      __syncwarp();
     }
   }
   for (int j = 0; j < n_tiles && ok; ++j) {
@@ -254,18 +239,14 @@ __device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int
     }
     tc_fence_after();
     issue_pv(1, st, j);
-    if (lane == 0) umma_commit(&sm.bar_vfree[st]);
+    if (lane == 0) umma_commit(&sm.bar_empty[st]);
     __syncwarp();
-    if (more) {
-      issue_s(1, st1);
-      if (lane == 0) umma_commit(&sm.bar_kfree[st1]);
-      __syncwarp();
-    }
+    if (more) issue_s(1, st1);
     done = j + 1;
   }
   if (!ok) atomicOr(&g_attn_error, 2u);
   // every MMA issued so far has finished before TMEM can be released
-  if (done > 0 && lane == 0) mbar_wait(&sm.bar_vfree[(done - 1) & 1], ((done - 1) >> 1) & 1);
+  if (done > 0 && lane == 0) mbar_wait(&sm.bar_empty[(done - 1) & 1], ((done - 1) >> 1) & 1);
 }
 
 // ---- softmax + epilogue (warps 0-3: head A, 4-7: head B) ------------------------
@@ -450,8 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_con
       mbar_init(&sm.bar_k[i], 1);
       mbar_init(&sm.bar_v[i], 1);
       mbar_init(&sm.bar_bias[i], 32);
-      mbar_init(&sm.bar_kfree[i], 1);
-      mbar_init(&sm.bar_vfree[i], 1);
+      mbar_init(&sm.bar_empty[i], 1);
       mbar_init(&sm.bar_s[i], 1);
       mbar_init(&sm.bar_p[i], 128);
       mbar_init(&sm.bar_o[i], 1);
