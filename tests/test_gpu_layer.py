@@ -128,3 +128,29 @@ def test_layer_host_buffers_match_device_path():
         assert torch.equal(o, w)
     with pytest.raises(ValueError):
         layer(pinned[0][0][:, :4], pinned[0][1], pinned[0][2])
+
+
+@pytest.mark.slow
+def test_layer_1m_variable_budgets_sampled():
+    """1M-token layer (8 x 131072, 32/8 heads, window 2048, budgets drawn from
+    {256, 512, 1024, 2048} with seed 1): the whole layer runs on the GPU; KV
+    head 0 (query heads 0-3) of blocks 0-2 is recomputed by the oracle on
+    sampled rows (the layer is independent across KV heads)."""
+    from dcc_kv_b200.workloads import layer_inputs, variable_budgets
+    nb, L, hq, hkv, d = 8, 131072, 32, 8, 128
+    budgets = variable_budgets(nb)
+    q, k, v = layer_inputs(nb, L, hq, hkv, d, device="cuda")
+    layer = dk.DccKvSyncLayer(nb, L, hq, hkv, d, budgets, window=2048)
+    out = layer(q, k, v)
+    torch.cuda.synchronize()
+    assert_no_device_timeouts()
+    assert torch.isfinite(out).all()
+    sub = [0, 1, 2]
+    rows = {b: np.array([0, 1, 2047, 2048, 77777, L - 1]) for b in sub}
+    qh = q[sub, 0:4].cpu()
+    kh, vh = k[sub, 0:1].cpu(), v[sub, 0:1].cpu()
+    ref, _ = _oracle_layer(qh, kh, vh, {(s, r): budgets[(s, r)] for r in sub for s in range(r)}, 2048, 64, 32,
+                           rows=rows)
+    for r in sub:
+        got = np64(out[r, 0:4][:, rows[r]])
+        assert rel_err(got, ref[r]) < 2e-2, r
