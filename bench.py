@@ -292,21 +292,12 @@ def run_gpu(args):
     a_launches = len(attn_ev[0])
     clocks = clk.summary()
     # end to end through the public layer call: pinned host inputs in, output
-    # back to host; the single-GPU layer pipelines the copies per block
+    # back to host; the layers pipeline the copies with the compute
     hq_, hk_, hv_ = (t.cpu().pin_memory() for t in (q, k, v))
     out_host = torch.empty(q.shape, dtype=q.dtype).pin_memory()
-    host_api = ws == 1
-    if not host_api:
-        dq, dk_, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
 
     def e2e_step():
-        if host_api:
-            layer(hq_, hk_, hv_, out=out_host)
-        else:
-            dq.copy_(hq_, non_blocking=True)
-            dk_.copy_(hk_, non_blocking=True)
-            dv.copy_(hv_, non_blocking=True)
-            out_host.copy_(layer(dq, dk_, dv), non_blocking=True)
+        layer(hq_, hk_, hv_, out=out_host)
 
     for _ in range(warmup):
         e2e_step()

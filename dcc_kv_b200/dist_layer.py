@@ -195,44 +195,138 @@ class DistributedDccKvLayer:
                 self.merge_rows.append(li)
         self._bound = key
 
-    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+    def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
+        """Local blocks q [n_local, H_q, L, d], k / v [n_local, H_kv, L, d] ->
+        their outputs.  Device inputs: returns an internal buffer.  Host
+        inputs (CPU, pinned for overlap): the copies are pipelined with the
+        compute and ``out`` (or an internal pinned buffer) is returned,
+        complete once the current stream is synchronized."""
         exp_q = (self.n_local, self.hq, self.L, self.d)
         exp_kv = (self.n_local, self.hkv, self.L, self.d)
         if tuple(q.shape) != exp_q or tuple(k.shape) != exp_kv or tuple(v.shape) != exp_kv:
             raise ValueError(f"expected local q {exp_q}, k/v {exp_kv}")
+        host = not q.is_cuda
         for t in (q, k, v):
-            if t.dtype != self.dtype or not t.is_contiguous() or t.device != self.device:
-                raise ValueError(f"inputs must be contiguous {self.dtype} on {self.device}")
+            if t.dtype != self.dtype or not t.is_contiguous() or (not host and t.device != self.device) or \
+                    (host and t.is_cuda):
+                raise ValueError(f"inputs must be contiguous {self.dtype}, all on {self.device} or all on the host")
+        if host:
+            return self._forward_host(q, k, v, out)
         self._bind(q, k, v)
+        self._run()
+        return self.o_loc
+
+    __call__ = forward
+
+    def _attention(self, problems) -> None:
         dev = self.device
         main = torch.cuda.current_stream(dev)
-        side = self.comm_stream
-        side.wait_stream(main)  # inputs written, previous step's buffers released
-        with torch.cuda.stream(side):
-            select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
-            dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.group)
-            run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
-            ns, nr = sum(self.send_splits), sum(self.recv_splits)
-            dist.all_to_all_single(self.recv_buf[:nr], self.send_buf[:ns], output_split_sizes=self.recv_splits,
-                                   input_split_sizes=self.send_splits, group=self.group)
-        # local causal attention meanwhile, on the main stream
-        scale = 1.0 / math.sqrt(self.d)
         ev = None
         if self.timing_events:
             ev = (torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             self.timing_events[self.timing_index].append(ev)
             ev[0].record(main)
-        run_attention(self.local_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
+        run_attention(problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code, dev)
         if ev is not None:
             ev[1].record(main)
-        main.wait_stream(side)
-        run_attention(self.compact_problems, self.hq, self.hkv, self.d, scale, self.code, dev)
-        for li in self.merge_rows:
-            merge_lse([self.o_loc[li], self.o_c[li]], [self.lse_loc[li], self.lse_c[li]], out=self.o_loc[li],
-                      want_lse=False)
-        return self.o_loc
 
-    __call__ = forward
+    def _run(self, windows_ready=None, kv_ready=None, q_ready=None, merged=None) -> None:
+        """One forward on bound buffers.  The optional per-phase events gate
+        the work on host-to-device copies (pooling on the query windows,
+        builds on K / V, local attention of block li on its queries) and
+        ``merged[li]`` is recorded once block li's output is final."""
+        dev = self.device
+        main = torch.cuda.current_stream(dev)
+        side = self.comm_stream
+        side.wait_stream(main)  # inputs written, previous step's buffers released
+        with torch.cuda.stream(side):
+            if windows_ready is not None:
+                side.wait_event(windows_ready)
+            select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
+            dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.group)
+            if kv_ready is not None:
+                side.wait_event(kv_ready)
+            run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
+            ns, nr = sum(self.send_splits), sum(self.recv_splits)
+            dist.all_to_all_single(self.recv_buf[:nr], self.send_buf[:ns], output_split_sizes=self.recv_splits,
+                                   input_split_sizes=self.send_splits, group=self.group)
+        # local causal attention meanwhile, on the main stream
+        if q_ready is None:
+            self._attention(self.local_problems)
+        else:
+            main.wait_event(kv_ready)
+            for li in range(self.n_local):
+                main.wait_event(q_ready[li])
+                self._attention([self.local_problems[li]])
+        main.wait_stream(side)
+        run_attention(self.compact_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code, dev)
+        for li in range(self.n_local):
+            if li in self.merge_rows:
+                merge_lse([self.o_loc[li], self.o_c[li]], [self.lse_loc[li], self.lse_c[li]], out=self.o_loc[li],
+                          want_lse=False)
+            if merged is not None:
+                merged[li].record(main)
+
+    def _forward_host(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out) -> torch.Tensor:
+        """Host buffers in and out.  Copy-in order: the destination windows of
+        every local block (pooling starts on them), then K and V (the builds),
+        then the remaining query rows block by block (local attention of a
+        block starts when its queries are in); each block's output is copied
+        out as soon as its merge is done."""
+        exp_q = (self.n_local, self.hq, self.L, self.d)
+        if out is None:
+            if getattr(self, "_host_out", None) is None:
+                self._host_out = torch.empty(exp_q, dtype=self.dtype).pin_memory()
+            out = self._host_out
+        elif out.is_cuda or tuple(out.shape) != exp_q or out.dtype != self.dtype or not out.is_contiguous():
+            raise ValueError(f"out must be a contiguous CPU {self.dtype} tensor of shape {exp_q}")
+        dev = self.device
+        if getattr(self, "_staging", None) is None:
+            self._staging = (torch.empty_like(q, device=dev), torch.empty_like(k, device=dev),
+                             torch.empty_like(v, device=dev))
+            self._h2d = torch.cuda.Stream(device=dev)
+            self._d2h = torch.cuda.Stream(device=dev)
+            self._ev_win, self._ev_kv = torch.cuda.Event(), torch.cuda.Event()
+            self._ev_q = [torch.cuda.Event() for _ in range(self.n_local)]
+            self._ev_merged = [torch.cuda.Event() for _ in range(self.n_local)]
+            self._ev_drained = [torch.cuda.Event() for _ in range(self.n_local)]
+            self._ev_done = None
+        dq, dk_, dv = self._staging
+        self._bind(dq, dk_, dv)
+        main = torch.cuda.current_stream(dev)
+        h2d, d2h = self._h2d, self._d2h
+        W = self.window
+        # the previous call's kernels must be done with the staging buffers,
+        # and its copy-out with the output buffers
+        if self._ev_done is None:
+            self._ev_done = torch.cuda.Event()
+            h2d.wait_stream(main)
+        else:
+            h2d.wait_event(self._ev_done)
+        for li in range(self.n_local):
+            main.wait_event(self._ev_drained[li])
+        with torch.cuda.stream(h2d):
+            for li in range(self.n_local):
+                for h in range(self.hq):
+                    dq[li, h, :W].copy_(q[li, h, :W], non_blocking=True)
+            self._ev_win.record(h2d)
+            dk_.copy_(k, non_blocking=True)
+            dv.copy_(v, non_blocking=True)
+            self._ev_kv.record(h2d)
+            for li in range(self.n_local):
+                if W < self.L:
+                    for h in range(self.hq):
+                        dq[li, h, W:].copy_(q[li, h, W:], non_blocking=True)
+                self._ev_q[li].record(h2d)
+        self._run(self._ev_win, self._ev_kv, self._ev_q, self._ev_merged)
+        self._ev_done.record(main)
+        with torch.cuda.stream(d2h):
+            for li in range(self.n_local):
+                d2h.wait_event(self._ev_merged[li])
+                out[li].copy_(self.o_loc[li], non_blocking=True)
+                self._ev_drained[li].record(d2h)
+        main.wait_stream(d2h)
+        return out
 
     def launches_per_forward(self) -> int:
         sets = len(self.sets)

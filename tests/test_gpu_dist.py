@@ -1,7 +1,8 @@
 """The sharded layer on 2+ GPUs (one process per GPU, NCCL) against the
 single-GPU layer on the same inputs: every rank's blocks agree within the
 bf16 bar (2e-2); the two differ only in how the compact blocks are split
-into KV tiles.  Skipped on a box with fewer than 2 GPUs."""
+into KV tiles.  The host-buffer call must reproduce the device call bit for
+bit.  Skipped on a box with fewer than 2 GPUs."""
 from __future__ import annotations
 
 import multiprocessing as pymp
@@ -43,6 +44,14 @@ def _worker(rank, world, port, errq):
         for li, b in enumerate(mine):
             err = ((out[li].float() - ref[b].float()).abs().max() / ref[b].float().abs().max()).item()
             assert err < 2e-2, f"block {b}: {err}"
+        # host buffers: copies pipelined with the compute, same kernels, same result
+        want = out.cpu()
+        hq, hk, hv = (t[mine].contiguous().pin_memory() for t in (q, k, v))
+        host_out = torch.empty(want.shape, dtype=want.dtype).pin_memory()
+        for _ in range(2):
+            layer(hq, hk, hv, out=host_out)
+        torch.cuda.synchronize()
+        assert torch.equal(host_out, want)
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
