@@ -279,6 +279,138 @@ __global__ void __launch_bounds__(TPB) fps_cluster_kernel(const __grid_constant_
   }
 }
 
+// ---- FPS for bf16 query sets: fp32 points, PPT per thread ------------------------
+// The same step as fps_cluster_kernel with the projected points rounded to
+// fp32 (the FP64 projection and normalisation are unchanged): half the
+// registers per point, so a set of 8192 points needs a cluster of 8 CTAs
+// instead of 16 and twice as many sets run at once.  Distances are fp32, so
+// two candidates closer than fp32 resolution may be ordered differently from
+// the FP64 oracle; the bf16 path is held to its output tolerance, not to
+// index equality.
+__device__ __forceinline__ unsigned order_key32(float v) {
+  const int b = __float_as_int(v + 0.f);
+  return b >= 0 ? (unsigned)b | 0x80000000u : ~(unsigned)b;
+}
+__device__ __forceinline__ void warp_argmax_key32(unsigned& key, int& idx) {
+  const unsigned hi = __reduce_max_sync(0xffffffffu, key);
+  idx = (int)__reduce_min_sync(0xffffffffu, key == hi ? (unsigned)idx : 0x7fffffffu);
+  key = hi;
+}
+
+template <int DPP>
+struct ClusterSlot32 {
+  unsigned key;
+  int i;
+  float coords[DPP];
+};
+
+template <typename T, int DPP, int TPB, int PPT>
+__global__ void __launch_bounds__(TPB) fps_cluster32_kernel(const __grid_constant__ SetBatch b, int M, int d) {
+  cg::cluster_group cluster = cg::this_cluster();
+  const int cl = (int)cluster.num_blocks();
+  const int rank = (int)cluster.block_rank();
+  const SetDesc& s = b.p[blockIdx.x / cl];
+  constexpr int NW = TPB / 32;
+  __shared__ unsigned wkey[NW];
+  __shared__ int widx[NW];
+  __shared__ float wcoords[NW][DPP];
+  __shared__ ClusterSlot32<DPP> cslot[2][16];
+  __shared__ float ystart[DPP];
+  __shared__ int sel[256];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  float x[PPT][DPP];
+  float mind[PPT];
+  int pid[PPT];
+#pragma unroll
+  for (int q = 0; q < PPT; ++q) {
+    pid[q] = rank * TPB * PPT + q * TPB + threadIdx.x;  // consecutive threads, consecutive points
+    const bool valid = pid[q] < s.n;
+#pragma unroll
+    for (int k = 0; k < DPP; ++k) x[q][k] = valid ? (float)s.normed[(int64_t)pid[q] * DPP + k] : 0.f;
+  }
+  if (threadIdx.x < DPP) ystart[threadIdx.x] = (float)s.normed[s.start * DPP + threadIdx.x];
+  if (threadIdx.x == 0) sel[0] = (int)s.start;
+  __syncthreads();
+  auto dist_to = [&](int q, const float* y) {
+    float dp4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int k = 0; k < DPP; ++k) dp4[k & 3] = fmaf(x[q][k], y[k], dp4[k & 3]);
+    return 1.f - ((dp4[0] + dp4[1]) + (dp4[2] + dp4[3]));
+  };
+#pragma unroll
+  for (int q = 0; q < PPT; ++q) mind[q] = pid[q] < s.n ? dist_to(q, ystart) : -INFINITY;
+  for (int t = 1; t < M; ++t) {
+    const int par = t & 1;
+    // this thread's best point (larger distance, then lower index)
+    unsigned key = order_key32(mind[0]);
+    int bi = pid[0] < s.n ? pid[0] : 0x7fffffff;
+    int bq = 0;
+#pragma unroll
+    for (int q = 1; q < PPT; ++q) {
+      const unsigned kq = order_key32(mind[q]);
+      if (pid[q] < s.n && kq > key) {
+        key = kq;
+        bi = pid[q];
+        bq = q;
+      }
+    }
+    const int my_i = bi;
+    warp_argmax_key32(key, bi);
+    if (my_i == bi && bi != 0x7fffffff) {
+#pragma unroll
+      for (int q = 0; q < PPT; ++q)
+        if (q == bq) {
+#pragma unroll
+          for (int k = 0; k < DPP; ++k) wcoords[warp][k] = x[q][k];
+        }
+    }
+    if (lane == 0) {
+      wkey[warp] = key;
+      widx[warp] = bi;
+    }
+    __syncthreads();
+    if (warp == 0) {
+      unsigned ck = lane < NW ? wkey[lane] : 0u;
+      int ci = lane < NW ? widx[lane] : 0x7fffffff;
+      const int mine = ci;
+      warp_argmax_key32(ck, ci);
+      const int bw = __ffs(__ballot_sync(0xffffffffu, lane < NW && mine == ci)) - 1;
+      for (int dst = 0; dst < cl; ++dst) {
+        ClusterSlot32<DPP>* rs = cluster.map_shared_rank(&cslot[par][rank], dst);
+        if (lane < DPP) rs->coords[lane] = wcoords[bw][lane];
+        if (DPP > 32 && lane + 32 < DPP) rs->coords[lane + 32] = wcoords[bw][lane + 32];
+        if (lane == 0) {
+          rs->key = ck;
+          rs->i = ci;
+        }
+      }
+    }
+    if (cl > 1) cluster.sync(); else __syncthreads();
+    unsigned gk = lane < cl ? cslot[par][lane].key : 0u;
+    int gi = lane < cl ? cslot[par][lane].i : 0x7fffffff;
+    const int my_gi = gi;
+    warp_argmax_key32(gk, gi);
+    const int gw = __ffs(__ballot_sync(0xffffffffu, lane < cl && my_gi == gi)) - 1;
+    if (threadIdx.x == 0) sel[t] = gi;
+    const float* y = cslot[par][gw].coords;
+#pragma unroll
+    for (int q = 0; q < PPT; ++q)
+      if (pid[q] < s.n) mind[q] = fminf(mind[q], dist_to(q, y));
+  }
+  // keep this CTA's shared memory alive until every remote access finished
+  if (cl > 1) cluster.sync();
+  if (rank == 0) {
+    for (int t = threadIdx.x; t < M; t += TPB) s.out_idx[t] = sel[t];
+    if (s.out_repr == nullptr) return;
+    const T* q = static_cast<const T*>(s.q);
+    T* out = static_cast<T*>(s.out_repr);
+    for (int e = threadIdx.x; e < M * d; e += TPB) {
+      const int t = e / d, c = e - t * d;
+      out[e] = q[set_row_offset(s, sel[t]) + c];
+    }
+  }
+}
+
 // ---- FPS from global memory: any N (one CTA per set) --------------------------
 template <typename T, int DPP>
 __global__ void __launch_bounds__(1024) fps_global_kernel(const __grid_constant__ SetBatch b, int M,
@@ -361,13 +493,15 @@ static int dpp_for(int dp) { return dp <= 8 ? 8 : dp <= 16 ? 16 : dp <= 32 ? 32 
 
 template <typename T, int DPP>
 static int run_fps(SetBatch& b, int M, int d, int max_n, cudaStream_t st) {
-  // register path: T threads per CTA, up to 16 CTAs per cluster
+  // register path: T threads per CTA, up to 16 CTAs per cluster; bf16 sets
+  // keep fp32 points, two per thread
   constexpr int TPB = DPP <= 32 ? 512 : 256;
-  const int cl = (max_n + TPB - 1) / TPB;
+  constexpr int PPT = std::is_same<T, __nv_bfloat16>::value ? 2 : 1;
+  const int cl = (max_n + TPB * PPT - 1) / (TPB * PPT);
   if (cl <= 16) {
     int clp = 1;
     while (clp < cl) clp <<= 1;  // power-of-two cluster
-    auto kern = fps_cluster_kernel<T, DPP, TPB>;
+    auto kern = PPT == 2 ? fps_cluster32_kernel<T, DPP, TPB, 2> : fps_cluster_kernel<T, DPP, TPB>;
     if (clp > 8) {
       DCC_CHECK(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1),
                            "fps: allow cluster 16"));
