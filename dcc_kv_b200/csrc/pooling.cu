@@ -96,49 +96,68 @@ __device__ __forceinline__ void project_accumulate(double* z, const double* pm_c
     z[k + 1] = fma(pv.y, qc, z[k + 1]);
   }
 }
+template <int DPP>
+__device__ __forceinline__ void project_accumulate(float* z, const float* pm_c, float qc) {
+#pragma unroll
+  for (int k = 0; k < DPP; k += 4) {
+    const float4 pv = *reinterpret_cast<const float4*>(pm_c + k);
+    z[k] = fmaf(pv.x, qc, z[k]);
+    z[k + 1] = fmaf(pv.y, qc, z[k + 1]);
+    z[k + 2] = fmaf(pv.z, qc, z[k + 2]);
+    z[k + 3] = fmaf(pv.w, qc, z[k + 3]);
+  }
+}
+
+// Projection arithmetic: FP64 for fp32 / fp64 query sets (the parity path:
+// FPS argmax identical to the FP64 reference), fp32 for bf16 sets, whose FPS
+// runs on fp32 points anyway.
+template <typename T> struct ProjAcc { using A = double; };
+template <> struct ProjAcc<__nv_bfloat16> { using A = float; };
 
 template <typename T, int DPP>
 __global__ void __launch_bounds__(128) project_kernel(const __grid_constant__ SetBatch b,
                                                       const __grid_constant__ ProjBits proj, int d,
                                                       int dp) {
-  extern __shared__ __align__(16) double pm[];  // [d][DPP]
+  using A = typename ProjAcc<T>::A;
+  extern __shared__ __align__(16) unsigned char pm_raw[];
+  A* pm = reinterpret_cast<A*>(pm_raw);  // [d][DPP]
   const SetDesc& s = b.p[blockIdx.y];
-  const double mag = (double)proj.mag;
+  const A mag = (A)proj.mag;
   for (int e = threadIdx.x; e < d * DPP; e += blockDim.x) {
     const int c = e / DPP, k = e - c * DPP;
     const int bit = k * d + c;
-    pm[e] = k < dp ? (((proj.bits[bit >> 5] >> (bit & 31)) & 1u) ? mag : -mag) : 0.0;
+    pm[e] = k < dp ? (((proj.bits[bit >> 5] >> (bit & 31)) & 1u) ? mag : -mag) : (A)0;
   }
   __syncthreads();
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= s.n) return;
   const T* q = static_cast<const T*>(s.q) + set_row_offset(s, i);
-  double z[DPP];
+  A z[DPP];
 #pragma unroll
-  for (int k = 0; k < DPP; ++k) z[k] = 0.0;
+  for (int k = 0; k < DPP; ++k) z[k] = (A)0;
   if (d % 8 == 0 && (reinterpret_cast<uintptr_t>(q) & 15) == 0) {
     for (int c0 = 0; c0 < d; c0 += 8) {
       double qv[8];
       load8<T>(q + c0, qv);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) project_accumulate<DPP>(z, pm + (c0 + j) * DPP, qv[j]);
+      for (int j = 0; j < 8; ++j) project_accumulate<DPP>(z, pm + (c0 + j) * DPP, (A)qv[j]);
     }
   } else {
-    for (int c = 0; c < d; ++c) project_accumulate<DPP>(z, pm + c * DPP, load_row_elem<T>(q, c));
+    for (int c = 0; c < d; ++c) project_accumulate<DPP>(z, pm + c * DPP, (A)load_row_elem<T>(q, c));
   }
-  double ss = 0.0;
+  A ss = (A)0;
 #pragma unroll
   for (int k = 0; k < DPP; ++k) ss = fma(z[k], z[k], ss);
-  double inv = 1.0 / (sqrt(ss) + 1e-8);
-  ss = 0.0;
+  A inv = (A)1 / (sqrt(ss) + (A)1e-8);
+  ss = (A)0;
 #pragma unroll
   for (int k = 0; k < DPP; ++k) {
     z[k] = z[k] * inv;  // z / (||z|| + 1e-8), representative_query.py:108
     ss = fma(z[k], z[k], ss);
   }
-  inv = 1.0 / (sqrt(ss) + 1e-8);  // normalised again inside FPS, :63
+  inv = (A)1 / (sqrt(ss) + (A)1e-8);  // normalised again inside FPS, :63
 #pragma unroll
-  for (int k = 0; k < DPP; ++k) s.normed[i * DPP + k] = z[k] * inv;
+  for (int k = 0; k < DPP; ++k) s.normed[i * DPP + k] = (double)(z[k] * inv);
 }
 
 // Argmax keys: a double maps to a uint64 that orders like the double (larger
@@ -531,7 +550,7 @@ static int run_pooling(SetBatch& b, int d, int M, int dp, const ProjBits& proj, 
   // projection
   const int blocks_x = (max_n + 127) / 128;
   dim3 grid(blocks_x, b.n);
-  const size_t pm_bytes = (size_t)d * dpp * sizeof(double);
+  const size_t pm_bytes = (size_t)d * dpp * sizeof(typename ProjAcc<T>::A);
   auto launch = [&](auto kern) -> int {
     DCC_CHECK(check_cuda(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)pm_bytes),
                          "project smem"));
