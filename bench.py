@@ -394,8 +394,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", dest="cpu_baseline", action="store_false")
-    ap.add_argument("--schedule", choices=("pipelined", "batched"), default="pipelined",
-                    help="single-GPU layer schedule: builds overlapped with per-block attention, or in order")
+    ap.add_argument("--schedule", choices=("pipelined", "batched"), default="batched",
+                    help="single-GPU layer schedule: builds then one attention launch (default), or builds "
+                         "overlapped with per-block attention")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run two attention launches of one block (small case for ncu) and exit")
     args = ap.parse_args()
