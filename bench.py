@@ -88,29 +88,69 @@ def attention_traffic():
 
 
 class ClockSampler:
-    """nvidia-smi clocks and throttle reasons sampled during the timed region."""
+    """SM clock and clock-event reasons of this GPU, read through NVML every
+    millisecond on a host thread for the whole timed region (read-only
+    queries; falls back to nvidia-smi at 200 ms when NVML is unavailable)."""
 
+    # NVML clock-event reason bits (nvmlClocksEventReason*)
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
+        self.rows = []
+        self.max_mhz = None
+        self.thread = None
+        self.stop = None
         self.proc = None
         self.path = None
 
-    def __enter__(self):
-        fd, self.path = tempfile.mkstemp(suffix=".csv")
-        os.close(fd)
+    def _nvml_handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        uuid = str(torch.cuda.get_device_properties(self.index).uuid)
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
-        except OSError:
-            self.proc = None
+            return pynvml, pynvml.nvmlDeviceGetHandleByUUID(uuid if uuid.startswith("GPU-") else "GPU-" + uuid)
+        except Exception:
+            return pynvml, pynvml.nvmlDeviceGetHandleByIndex(self.index)
+
+    def __enter__(self):
+        import threading
+        try:
+            nv, h = self._nvml_handle()
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM))
+            self.stop = threading.Event()
+
+            def run():
+                while not self.stop.is_set():
+                    try:
+                        mhz = nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)
+                        mask = nv.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.rows.append((float(mhz), int(mask)))
+                    except Exception:
+                        pass
+                    self.stop.wait(0.001)
+
+            self.thread = threading.Thread(target=run, daemon=True)
+            self.thread.start()
+        except Exception:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            try:
+                self.proc = subprocess.Popen(
+                    ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.FIELDS}",
+                     "--format=csv,noheader,nounits", "-lms", "200"],
+                    stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+            except OSError:
+                self.proc = None
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -119,13 +159,19 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self):
+        if self.thread is not None:
+            if not self.rows:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unsampled"], "source": "nvml"}
+            reasons = sorted({name for _, mask in self.rows for bit, name in self.REASONS.items() if mask & bit})
+            return {"sm_mhz": statistics.median(m for m, _ in self.rows), "sm_max_mhz": self.max_mhz,
+                    "reasons": reasons, "samples": len(self.rows), "source": "nvml"}
         rows = []
         try:
             for line in open(self.path):
                 parts = [x.strip() for x in line.split(",")]
                 if len(parts) >= 9:
                     rows.append(parts)
-        except OSError:
+        except (OSError, TypeError):
             pass
         finally:
             if self.path:
@@ -137,7 +183,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
-                "reasons": reasons, "samples": len(rows)}
+                "reasons": reasons, "samples": len(rows), "source": "nvidia-smi"}
 
 
 def dist_env():

@@ -353,3 +353,85 @@ def full_causal_attention(q_full: np.ndarray, k_full: np.ndarray, v_full: np.nda
         p = softmax(s)
         out[i] = p @ np.asarray(v_full[: r + 1], F64)
     return out
+
+
+# ---------------------------------------------------------------------------
+# Shared-compaction baselines (src/baselines): one compact per source chunk,
+# used by every later query, with the reference's causal prefix on the compact
+# index (query r sees the first r + 1 - offset_s entries of chunk s's compact).
+# ---------------------------------------------------------------------------
+def _chunk_bounds(total: int, chunk_size: int, world_size: int):
+    """fast_kv_cpu.py:68-71 / apb_cpu.py:99-102: chunk s = [s * chunk, (s + 1) * chunk),
+    the last chunk runs to the end of the sequence."""
+    out = []
+    for s in range(world_size):
+        lo = s * chunk_size
+        hi = (s + 1) * chunk_size if s < world_size - 1 else total
+        out.append((lo, hi))
+    return out
+
+
+def _ring_over_compacts(queries, compacts, offsets, causal: bool):
+    """fast_kv_cpu.py:89-125 / apb_cpu.py:117-146: every query row merges one
+    online-softmax state per visible chunk; rows with none get zeros.
+    ``compacts``: list of (keys, values, bias or None)."""
+    q = np.asarray(queries, F64)
+    T, d = q.shape
+    dv = compacts[0][1].shape[-1]
+    out = np.zeros((T, dv))
+    scale = 1.0 / d ** 0.5
+    for r in range(T):
+        state = None
+        for (k, v, bias), off in zip(compacts, offsets):
+            if causal and off > r:
+                continue
+            n = min(r + 1 - off, k.shape[0]) if causal else k.shape[0]
+            if n <= 0:
+                continue
+            logits = (np.asarray(k[:n], F64) @ q[r]) * scale
+            st = online_softmax_state(logits, np.asarray(v[:n], F64), None if bias is None else bias[:n])
+            state = st if state is None else merge_states(state, st)
+        if state is not None:
+            out[r] = state[2] / state[1]
+    return out
+
+
+def fast_kv(queries, keys, values, chunk_size: int, world_size: int, budget: int = 256,
+            num_repr_queries: int = 64, projection_dim: int = 32, lambda_beta: float = 1e-3,
+            lambda_value: float = 1e-3, seed: int = 42, causal: bool = True):
+    """fast_kv_cpu.py:35-125: each chunk is compacted once with ALL queries as
+    destination queries (min(budget, chunk) entries), then ring attention
+    over the compacts with their logit bias."""
+    T = queries.shape[0]
+    compacts, offsets = [], []
+    for lo, hi in _chunk_bounds(T, chunk_size, world_size):
+        c = build_compact_kv(keys[lo:hi], values[lo:hi], queries, min(budget, hi - lo), num_repr_queries,
+                             projection_dim, lambda_beta, lambda_value, seed)
+        compacts.append((c.keys, c.values, c.logit_bias))
+        offsets.append(lo)
+    return _ring_over_compacts(queries, compacts, offsets, causal)
+
+
+def select_anchor_blocks(keys, values, queries, budget: int):
+    """apb_cpu.py:36-61: the ``budget`` keys with the largest attention mass
+    sum_a softmax(q_a K^T / sqrt(d))[j] over the given queries (sorted by mass,
+    ties by lower index)."""
+    d = keys.shape[-1]
+    A = softmax((np.asarray(queries, F64) @ np.asarray(keys, F64).T) * (1.0 / d ** 0.5))
+    idx = topk_desc(A.sum(axis=0), budget)
+    return np.asarray(keys, F64)[idx], np.asarray(values, F64)[idx], idx
+
+
+def apb(queries, keys, values, chunk_size: int, world_size: int, anchor_budget: int = 128,
+        causal: bool = True):
+    """apb_cpu.py:64-152: anchors of chunk s chosen by the attention mass of
+    queries[offset_s:] (all queries if that is empty), then ring attention
+    over the anchors (no bias)."""
+    T = queries.shape[0]
+    compacts, offsets = [], []
+    for lo, hi in _chunk_bounds(T, chunk_size, world_size):
+        fut = queries[lo:] if T - lo > 0 else queries
+        ak, av, _ = select_anchor_blocks(keys[lo:hi], values[lo:hi], fut, min(anchor_budget, hi - lo))
+        compacts.append((ak, av, None))
+        offsets.append(lo)
+    return _ring_over_compacts(queries, compacts, offsets, causal)

@@ -2,7 +2,8 @@
 
 Run once in a container that holds the reference checkout (read-only):
 
-    python tests/golden/make_golden.py /root/reference
+    python tests/golden/make_golden.py /root/reference             # everything
+    python tests/golden/make_golden.py /root/reference baselines   # baselines_small.npz only
 
 It imports ``src.dcc_kv_ref`` from that checkout, applies the FP64 dtype shim
 to ``rademacher_projection`` (the reference casts the projection to float32,
@@ -185,5 +186,38 @@ def main(root: str) -> None:
     print("golden vectors written to", HERE)
 
 
+def baselines(root: str) -> None:
+    """Shared-compaction baselines (src/baselines/fast_kv_cpu.py, apb_cpu.py)
+    in float64 on ragged chunks (the last chunk shorter), causal and not."""
+    ref, _ = load_reference(root)
+    from src.baselines import fast_kv_cpu as _fk  # the package re-exports the functions
+    from src.baselines import apb_cpu as _apb
+    fast_kv_cpu = _fk if callable(_fk) else _fk.fast_kv_cpu
+    apb_cpu = _apb if callable(_apb) else _apb.apb_cpu
+    from src.baselines.fast_kv_cpu import FastKVConfig
+    from src.baselines.apb_cpu import APBConfig
+    g = torch.Generator().manual_seed(21)
+    T, d, chunk, world = 320, 32, 96, 4
+    Q = torch.randn(T, d, generator=g, dtype=torch.float64)
+    K = torch.randn(T, d, generator=g, dtype=torch.float64)
+    V = torch.randn(T, d, generator=g, dtype=torch.float64)
+    fcfg = FastKVConfig(budget=24, num_repr_queries=16, projection_dim=8)
+    acfg = APBConfig(anchor_budget=20)
+    # inputs are not stored: tests redraw them (CPU generator, seed 21, T x d float64: Q, K, V);
+    # outputs are stored as float32 (the bar is 1e-4 relative)
+    out = dict(seed=21, T=T, d=d, chunk=chunk, world=world, fk_budget=24, fk_M=16, fk_dp=8, apb_budget=20)
+    for causal in (True, False):
+        tag = "causal" if causal else "full"
+        out[f"fastkv_{tag}"] = fast_kv_cpu(Q, K, V, chunk, world, fcfg, causal=causal).float().numpy()
+        out[f"apb_{tag}"] = apb_cpu(Q, K, V, chunk, world, acfg, causal=causal).float().numpy()
+    np.savez_compressed(os.path.join(HERE, "baselines_small.npz"), **out)
+    print("baseline golden vectors written to", HERE)
+
+
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) > 2 and sys.argv[2] == "baselines":
+        baselines(root)
+    else:
+        main(root)
+        baselines(root)

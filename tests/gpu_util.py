@@ -47,3 +47,11 @@ def assert_no_device_timeouts():
     from dcc_kv_b200 import _lib as L
     assert L.lib().dcc_device_error_status(1) == 0, "attention: a bounded device wait expired"
     assert L.lib().dcc_build_error_status(1) == 0, "scoring: a bounded device wait expired"
+
+
+def baseline_inputs(f):
+    """Q, K, V of the baseline fixtures: drawn again with torch's CPU generator
+    (seed from the fixture, T x d float64, in that order)."""
+    g = torch.Generator().manual_seed(int(f["seed"]))
+    T, d = int(f["T"]), int(f["d"])
+    return tuple(torch.randn(T, d, generator=g, dtype=torch.float64) for _ in range(3))

@@ -120,3 +120,18 @@ def test_small_layer_matches_reference():
             for g in range(f["K"].shape[1]):
                 np.testing.assert_array_equal(comp[(s, r, g)].selected_indices[:16], f["sel"][k][g])
             k += 1
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_shared_compaction_baselines_match_reference(causal):
+    """FastKV (one compact per chunk from all queries) and APB (anchors by
+    attention mass) against the reference's own baseline functions."""
+    from gpu_util import baseline_inputs
+    f = _load("baselines_small.npz")
+    Q, K, V = (x.numpy() for x in baseline_inputs(f))
+    tag = "causal" if causal else "full"
+    fk = orc.fast_kv(Q, K, V, int(f["chunk"]), int(f["world"]), int(f["fk_budget"]), int(f["fk_M"]),
+                     int(f["fk_dp"]), causal=causal)
+    ap = orc.apb(Q, K, V, int(f["chunk"]), int(f["world"]), int(f["apb_budget"]), causal=causal)
+    for got, want in ((fk, f[f"fastkv_{tag}"]), (ap, f[f"apb_{tag}"])):
+        assert np.abs(got - want).max() / np.abs(want).max() < 1e-6
