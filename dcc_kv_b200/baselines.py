@@ -121,3 +121,64 @@ def apb(queries: torch.Tensor, keys: torch.Tensor, values: torch.Tensor, chunk_s
         compacts.append((ak, av, None))
         offsets.append(lo)
     return _ring_over_compacts(queries, compacts, offsets, causal)
+
+
+# ---------------------------------------------------------------------------
+# Ring attention (src/baselines/ring_attention_cpu.py): exact attention over
+# the whole context, chunk by chunk, merged by online softmax.
+# ---------------------------------------------------------------------------
+def ring_attention(queries: torch.Tensor, keys_chunks: Sequence[torch.Tensor],
+                   values_chunks: Sequence[torch.Tensor], causal: bool = True) -> torch.Tensor:
+    """ring_attention_cpu.py:24-82 on one GPU: queries [L, d_h] see the
+    concatenated chunks (row r the keys at positions <= r when causal) -- one
+    attention launch over the chunks as KV segments (causal on the
+    concatenation), the same online softmax the reference folds per chunk."""
+    L.require_cuda(queries, *keys_chunks, *values_chunks)
+    k = torch.cat(list(keys_chunks), dim=0)
+    v = torch.cat(list(values_chunks), dim=0)
+    o, _ = attention(queries[None], [(k[None], v[None], None)], causal=causal)
+    return o[0]
+
+
+def dist_ring_attention(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, group=None,
+                        causal: bool = True) -> torch.Tensor:
+    """Ring attention over NCCL: rank s holds chunk s (q, k, v [L_s, d] with
+    equal L_s on every rank).  Step i attends the local queries to the chunk
+    of rank s - i (causal for i = 0, skipped for later chunks when causal)
+    while the next chunk travels one hop around the ring (batched isend /
+    irecv on a side stream); the partials are merged by one P-way LSE merge.
+    Every rank takes the same communication steps."""
+    import torch.distributed as dist
+    L.require_cuda(q, k, v)
+    rank, world = dist.get_rank(group), dist.get_world_size(group)
+    dev = q.device
+    main = torch.cuda.current_stream(dev)
+    comm = torch.cuda.Stream(device=dev)
+    cur = torch.cat([k, v], dim=1).contiguous()  # one buffer per hop: [L_s, d_k + d_v]
+    nxt = torch.empty_like(cur)
+    dk = k.shape[1]
+    outs, lses = [], []
+    nxt_rank, prv_rank = (rank + 1) % world, (rank - 1) % world
+    if group is not None:
+        nxt_rank = dist.get_global_rank(group, nxt_rank)
+        prv_rank = dist.get_global_rank(group, prv_rank)
+    for i in range(world):
+        src = (rank - i) % world
+        reqs = []
+        if i + 1 < world:
+            comm.wait_stream(main)  # cur is complete, nxt is free
+            with torch.cuda.stream(comm):
+                ops = [dist.P2POp(dist.isend, cur, nxt_rank, group), dist.P2POp(dist.irecv, nxt, prv_rank, group)]
+                reqs = dist.batch_isend_irecv(ops)
+        if not causal or src <= rank:
+            seg = [(cur[None, :, :dk], cur[None, :, dk:], None)]
+            o, lse = attention(q[None], seg, causal=causal and src == rank)
+            outs.append(o[0])
+            lses.append(lse[0])
+        for r in reqs:
+            r.wait()
+        if i + 1 < world:
+            main.wait_stream(comm)
+            cur, nxt = nxt, cur
+    out, _ = merge_lse(outs, lses, want_lse=False)
+    return out

@@ -194,6 +194,7 @@ def baselines(root: str) -> None:
     from src.baselines import apb_cpu as _apb
     fast_kv_cpu = _fk if callable(_fk) else _fk.fast_kv_cpu
     apb_cpu = _apb if callable(_apb) else _apb.apb_cpu
+    from src.baselines.ring_attention_cpu import ring_attention_cpu
     from src.baselines.fast_kv_cpu import FastKVConfig
     from src.baselines.apb_cpu import APBConfig
     g = torch.Generator().manual_seed(21)
@@ -210,6 +211,9 @@ def baselines(root: str) -> None:
         tag = "causal" if causal else "full"
         out[f"fastkv_{tag}"] = fast_kv_cpu(Q, K, V, chunk, world, fcfg, causal=causal).float().numpy()
         out[f"apb_{tag}"] = apb_cpu(Q, K, V, chunk, world, acfg, causal=causal).float().numpy()
+        bounds = [(s * chunk, (s + 1) * chunk if s < world - 1 else T) for s in range(world)]
+        out[f"ring_{tag}"] = ring_attention_cpu(Q, [K[a:b] for a, b in bounds], [V[a:b] for a, b in bounds],
+                                                causal=causal).float().numpy()
     np.savez_compressed(os.path.join(HERE, "baselines_small.npz"), **out)
     print("baseline golden vectors written to", HERE)
 

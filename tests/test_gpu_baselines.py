@@ -1,4 +1,4 @@
-"""GPU parity of the shared-compaction baselines (FastKV, APB) against the
+"""GPU parity of the baselines (FastKV, APB, ring attention) against the
 reference's own baseline functions (golden vectors) and the oracle.
 
 * float64 inputs: the golden outputs within 1e-4 relative;
@@ -59,3 +59,22 @@ def test_anchor_selection_matches_oracle():
     ak, _ = bl.select_anchor_blocks(K[:96].to(dev()), V[:96].to(dev()), Q.to(dev()), budget)
     _, _, idx = orc.select_anchor_blocks(K[:96].numpy(), V[:96].numpy(), Q.numpy(), budget)
     np.testing.assert_array_equal(np64(ak), K[:96].numpy()[idx])
+
+
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("dtype", [torch.float64, torch.bfloat16])
+def test_ring_attention(dtype, causal):
+    f = golden("baselines_small.npz")
+    Q, K, V = baseline_inputs(f)
+    chunk, world, T = int(f["chunk"]), int(f["world"]), int(f["T"])
+    bounds = [(s * chunk, (s + 1) * chunk if s < world - 1 else T) for s in range(world)]
+    q, k, v = (x.to(dtype).to(dev()) for x in (Q, K, V))
+    got = bl.ring_attention(q, [k[a:b] for a, b in bounds], [v[a:b] for a, b in bounds], causal=causal)
+    torch.cuda.synchronize()
+    if dtype == torch.float64:
+        want, tol = f["ring_causal" if causal else "ring_full"], 1e-4
+    else:
+        Qr, Kr, Vr = (x.to(dtype).double().numpy() for x in (Q, K, V))
+        want = orc.attention_partial(Qr, Kr, Vr, positions=np.arange(T) if causal else None)[0]
+        tol = 2e-2
+    assert rel_err(np64(got), want) < tol

@@ -77,3 +77,52 @@ def test_distributed_layer_matches_single_gpu():
         errors.append(errq.get())
     assert not errors, "\n".join(errors)
     assert all(p.exitcode == 0 for p in procs)
+
+
+def _ring_worker(rank, world, port, errq):
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        from dcc_kv_b200 import baselines as bl
+        g = torch.Generator().manual_seed(5)
+        T, d = 256 * world, 128
+        q, k, v = (torch.randn(T, d, generator=g).to(torch.bfloat16) for _ in range(3))
+        c = T // world
+        lo, hi = rank * c, (rank + 1) * c
+        for causal in (True, False):
+            got = bl.dist_ring_attention(q[lo:hi].to(dev), k[lo:hi].to(dev), v[lo:hi].to(dev), causal=causal)
+            want = bl.ring_attention(q.to(dev), [k.to(dev)], [v.to(dev)], causal=causal)[lo:hi]
+            torch.cuda.synchronize()
+            err = ((got.float() - want.float()).abs().max() / want.float().abs().max()).item()
+            assert err < 2e-2, f"rank {rank} causal {causal}: {err}"
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put(traceback.format_exc())
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ring_attention_over_nccl_matches_single_gpu():
+    world = 2
+    ctx = pymp.get_context("spawn")
+    errq = ctx.Queue()
+    port = random.randint(20000, 40000)
+    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not errors, "\n".join(errors)
+    assert all(p.exitcode == 0 for p in procs)

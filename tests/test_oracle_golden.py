@@ -133,5 +133,8 @@ def test_shared_compaction_baselines_match_reference(causal):
     fk = orc.fast_kv(Q, K, V, int(f["chunk"]), int(f["world"]), int(f["fk_budget"]), int(f["fk_M"]),
                      int(f["fk_dp"]), causal=causal)
     ap = orc.apb(Q, K, V, int(f["chunk"]), int(f["world"]), int(f["apb_budget"]), causal=causal)
-    for got, want in ((fk, f[f"fastkv_{tag}"]), (ap, f[f"apb_{tag}"])):
+    # ring attention is exact attention over the concatenated chunks
+    T = Q.shape[0]
+    ring = orc.attention_partial(Q, K, V, positions=np.arange(T) if causal else None)[0]
+    for got, want in ((fk, f[f"fastkv_{tag}"]), (ap, f[f"apb_{tag}"]), (ring, f[f"ring_{tag}"])):
         assert np.abs(got - want).max() / np.abs(want).max() < 1e-6
