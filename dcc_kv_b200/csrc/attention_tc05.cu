@@ -485,7 +485,15 @@ int launch_attn_tc05(const dcc_attn_problem* probs, int n, const AttnParams& prm
     if (max_lq > 0) {
       dim3 grid((unsigned)((max_lq + 127) / 128), prm.n_q_heads / 2, b.n);
       attn_tc05_kernel<<<grid, kThreads, tc05_smem_bytes(), st>>>(b);
-      DCC_CHECK(check_launch("attn_tc05"));
+      const cudaError_t le = cudaGetLastError();
+      if (le != cudaSuccess) {
+        cudaFuncAttributes fa{};
+        cudaFuncGetAttributes(&fa, attn_tc05_kernel);
+        return fail(DCC_ERR_CUDA, std::string("attn_tc05 launch: ") + cudaGetErrorString(le) + " (" +
+                                      std::to_string(fa.numRegs) + " registers, max " +
+                                      std::to_string(fa.maxThreadsPerBlock) + " threads, " +
+                                      std::to_string(tc05_smem_bytes()) + " B dynamic shared memory)");
+      }
     }
     b.n = 0;
     max_lq = 0;

@@ -24,9 +24,6 @@ namespace dcc {
 
 constexpr int kCalTile = 64;
 
-template <typename TIn> struct CalStore { using T = float; };  // bf16 / fp32 values are exact in fp32
-template <> struct CalStore<double> { using T = double; };
-
 template <typename Acc>
 __device__ __forceinline__ int cal_bp(const BuildDesc<Acc>& p) {
   return (int)((int64_t)p.budget < p.L_s ? (int64_t)p.budget : p.L_s);
@@ -75,45 +72,51 @@ __device__ __forceinline__ void tile_gram(const double* zs, double* out) {
 }
 
 // ---- 1. logits, G, partial Gram of G --------------------------------------------------
+// The 64 x 64 logit tile accumulates over the head dimension in 64-column
+// halves staged as FP64 in shared memory (no conversion inside the FMA loop;
+// 2 x [64][65] doubles + the G tile keep two CTAs per SM).
 template <typename TIn, typename Acc>
 __global__ void __launch_bounds__(256) calib_logits_kernel(const __grid_constant__ BuildBatch<Acc> b,
                                                            const BuildParams prm) {
-  using ST = typename CalStore<TIn>::T;
   const BuildDesc<Acc>& p = b.p[blockIdx.y];
   const int Bp = cal_bp(p), M = p.M, d = prm.d;
   const int tile = blockIdx.x;
   if (tile >= p.n_btiles) return;
   const int b0 = tile * kCalTile;
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  const int ld = d + 1;
-  ST* qs = reinterpret_cast<ST*>(smem_raw);                  // [64][d+1]
-  ST* ks = qs + 64 * ld;                                       // [64][d+1]
-  double* gs = reinterpret_cast<double*>(smem_raw + ((2 * 64 * ld * sizeof(ST) + 15) / 16) * 16);  // [64][65]
+  double* qs = reinterpret_cast<double*>(smem_raw);  // [64][kLdG]: 64 columns of the head dim
+  double* ks = qs + 64 * kLdG;                       // [64][kLdG]
+  double* gs = ks + 64 * kLdG;                       // [64][kLdG]
   const TIn* rq = static_cast<const TIn*>(p.repr);
   const TIn* ck = static_cast<const TIn*>(p.out_keys);
-  for (int e = threadIdx.x; e < 64 * d; e += blockDim.x) {
-    const int r = e / d, c = e - r * d;
-    qs[r * ld + c] = r < M ? (ST)to_f64<TIn>(rq[r * d + c]) : (ST)0;
-    ks[r * ld + c] = b0 + r < Bp ? (ST)to_f64<TIn>(ck[(int64_t)(b0 + r) * d + c]) : (ST)0;
-  }
-  __syncthreads();
   const int ta = threadIdx.x & 15, tb = threadIdx.x >> 4;
   double acc[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
     for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
-  for (int c = 0; c < d; ++c) {
-    double qa[4], kb[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      qa[i] = (double)qs[(ta + 16 * i) * ld + c];
-      kb[i] = (double)ks[(tb + 16 * i) * ld + c];
+  for (int c0 = 0; c0 < d; c0 += 64) {
+    const int w = d - c0 < 64 ? d - c0 : 64;
+    __syncthreads();  // the previous half is consumed
+    for (int e = threadIdx.x; e < 64 * 64; e += blockDim.x) {
+      const int r = e >> 6, c = e & 63;
+      qs[r * kLdG + c] = (r < M && c < w) ? to_f64<TIn>(rq[r * d + c0 + c]) : 0.0;
+      ks[r * kLdG + c] = (b0 + r < Bp && c < w) ? to_f64<TIn>(ck[(int64_t)(b0 + r) * d + c0 + c]) : 0.0;
     }
+    __syncthreads();
+#pragma unroll 4
+    for (int c = 0; c < w; ++c) {
+      double qa[4], kb[4];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+      for (int i = 0; i < 4; ++i) {
+        qa[i] = qs[(ta + 16 * i) * kLdG + c];
+        kb[i] = ks[(tb + 16 * i) * kLdG + c];
+      }
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = fma(qa[i], kb[j], acc[i][j]);
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma(qa[i], kb[j], acc[i][j]);
+    }
   }
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -394,10 +397,9 @@ __global__ void __launch_bounds__(256) calib_cv_kernel(const __grid_constant__ B
 
 template <typename TIn, typename Acc>
 int launch_calibrate(const BuildBatch<Acc>& b, const BuildParams& prm, cudaStream_t st) {
-  using ST = typename CalStore<TIn>::T;
   int tmax = 1;
   for (int i = 0; i < b.n; ++i) tmax = b.p[i].n_btiles > tmax ? b.p[i].n_btiles : tmax;
-  const size_t smem1 = align_up(2 * 64 * (size_t)(prm.d + 1) * sizeof(ST), 16) + 64 * kLdG * sizeof(double);
+  const size_t smem1 = 3 * 64 * kLdG * sizeof(double);
   const size_t smem5 = (2 * 64 * kLdG + 64 * (size_t)(prm.dv + 1) + 3 * 64) * sizeof(double);
   const size_t smem6 = (64 * kLdG + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
   const size_t smem2 = (2 * 64 * kLdG + 6 * 64) * sizeof(double);
