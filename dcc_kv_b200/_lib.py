@@ -66,7 +66,8 @@ class dcc_attn_problem(C.Structure):
                 ("o", C.c_void_p), ("o_head_stride", C.c_int64), ("o_row_stride", C.c_int64),
                 ("lse", C.c_void_p), ("lse_head_stride", C.c_int64), ("Lq", C.c_int64),
                 ("n_seg", C.c_int32), ("causal", C.c_int32), ("causal_offset", C.c_int64),
-                ("seg", dcc_kv_segment * MAX_SEGMENTS)]
+                ("seg", dcc_kv_segment * MAX_SEGMENTS),
+                ("o_init", C.c_void_p), ("lse_init", C.c_void_p), ("lse_init_head_stride", C.c_int64)]
 
 
 _P = C.c_void_p
@@ -80,6 +81,7 @@ SIGNATURES = {
     "dcc_status_string": (C.c_char_p, [_I]),
     "dcc_last_error": (C.c_char_p, []),
     "dcc_version": (_I, []),
+    "dcc_struct_size": (_SZ, [C.c_char_p]),
     "dcc_rademacher_projection": (_I, [_I, _I, C.c_uint64, _P]),
     "dcc_fps_start_index": (_I64, [_I64, C.c_uint64]),
     "dcc_select_representative_queries_workspace_bytes": (_SZ, [_P, _I, _I, _I]),

@@ -34,8 +34,12 @@ def kv_segment(k: torch.Tensor, v: torch.Tensor, bias: Optional[torch.Tensor] = 
 
 def attn_problem(q: torch.Tensor, o: torch.Tensor, lse: Optional[torch.Tensor],
                  segments: Sequence[L.dcc_kv_segment], causal: bool = False,
-                 causal_offset: int = 0) -> L.dcc_attn_problem:
-    """q, o: [H_q, Lq, d] views (unit column stride); lse [H_q, Lq] float32."""
+                 causal_offset: int = 0, o_init: Optional[torch.Tensor] = None,
+                 lse_init: Optional[torch.Tensor] = None) -> L.dcc_attn_problem:
+    """q, o: [H_q, Lq, d] views (unit column stride); lse [H_q, Lq] float32.
+    ``o_init`` (o's strides, may be o itself) and ``lse_init`` [H_q, Lq]: an
+    initial online-softmax state the rows continue from (merge_softmax_states
+    of that state with the attention over the segments)."""
     if len(segments) > L.MAX_SEGMENTS:
         raise ValueError(f"at most {L.MAX_SEGMENTS} KV segments per problem")
     p = L.dcc_attn_problem()
@@ -53,6 +57,16 @@ def attn_problem(q: torch.Tensor, o: torch.Tensor, lse: Optional[torch.Tensor],
     p.causal_offset = causal_offset
     for i, s in enumerate(segments):
         p.seg[i] = s
+    if (o_init is None) != (lse_init is None):
+        raise ValueError("o_init and lse_init come together")
+    if o_init is not None:
+        if o_init.stride() != o.stride() or o_init.shape != o.shape or o_init.dtype != o.dtype:
+            raise ValueError("o_init must have o's shape, strides and dtype")
+        if lse_init.dtype != torch.float32 or lse_init.shape != o.shape[:2] or lse_init.stride(1) != 1:
+            raise ValueError("lse_init must be float32 [H_q, Lq] with unit row stride")
+        p.o_init = o_init.data_ptr()
+        p.lse_init = lse_init.data_ptr()
+        p.lse_init_head_stride = lse_init.stride(0)
     return p
 
 
@@ -68,9 +82,12 @@ def run_attention(problems: Sequence[L.dcc_attn_problem], n_q_heads: int, n_kv_h
 
 def attention(q: torch.Tensor, segments: Sequence[Tuple[torch.Tensor, torch.Tensor, Optional[torch.Tensor]]],
               causal: bool = False, causal_offset: int = 0,
-              scale: Optional[float] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+              scale: Optional[float] = None,
+              init: Optional[Tuple[torch.Tensor, torch.Tensor]] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """q [H_q, Lq, d]; segments: (k [H_kv, len, d], v, bias [H_kv, len] or None).
-    Returns (O [H_q, Lq, d] in q's dtype, LSE [H_q, Lq] float32)."""
+    Returns (O [H_q, Lq, d] in q's dtype, LSE [H_q, Lq] float32).  ``init`` =
+    (O0, LSE0) from an earlier call continues that online softmax: the result
+    is merge_softmax_states of the earlier state with these segments."""
     assert q.dim() == 3
     L.require_cuda(q)
     q = q.contiguous() if q.stride(-1) != 1 else q
@@ -88,6 +105,15 @@ def attention(q: torch.Tensor, segments: Sequence[Tuple[torch.Tensor, torch.Tens
         raise ValueError("need at least one KV segment")
     o = torch.empty_like(q)
     lse = torch.empty(hq, lq, dtype=torch.float32, device=q.device)
-    prob = attn_problem(q, o, lse, [kv_segment(k, v, b) for k, v, b in segs], causal, causal_offset)
+    o0 = lse0 = None
+    if init is not None:
+        o0, lse0 = init
+        L.require_cuda(o0, lse0)
+        o0 = o0.to(q.dtype).contiguous()
+        lse0 = lse0.to(torch.float32).contiguous()
+        if o0.shape != q.shape or lse0.shape != (hq, lq):
+            raise ValueError(f"init must be O {tuple(q.shape)} and LSE {(hq, lq)}")
+    prob = attn_problem(q, o, lse, [kv_segment(k, v, b) for k, v, b in segs], causal, causal_offset,
+                        o_init=o0, lse_init=lse0)
     run_attention([prob], hq, hkv, d, scale if scale is not None else 1.0 / math.sqrt(d), L.dtype_code(q), q.device)
     return o, lse

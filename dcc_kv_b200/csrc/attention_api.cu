@@ -23,12 +23,15 @@ extern "C" int dcc_attention_fwd(const dcc_attn_problem* problems, int n_problem
       return fail(DCC_ERR_INVALID_ARGUMENT, "attention_fwd: bad problem " + std::to_string(i));
     if (p.q_row_stride < head_dim || p.o_row_stride < head_dim)
       return fail(DCC_ERR_SHAPE, "attention_fwd: row stride smaller than head_dim");
-    mma = mma && aligned16(p.q) && aligned16(p.o) && p.q_row_stride % 8 == 0 &&
+    if ((p.o_init == nullptr) != (p.lse_init == nullptr))
+      return fail(DCC_ERR_INVALID_ARGUMENT, "attention_fwd: o_init and lse_init come together");
+    mma = mma && (!p.o_init || aligned16(p.o_init)) && aligned16(p.q) && aligned16(p.o) && p.q_row_stride % 8 == 0 &&
           p.q_head_stride % 8 == 0 && p.o_row_stride % 8 == 0 && p.o_head_stride % 8 == 0;
     for (int s = 0; s < p.n_seg; ++s) {
       const dcc_kv_segment& g = p.seg[s];
-      if (!g.k || !g.v || g.len < 0 || g.row_stride < head_dim)
+      if (g.len < 0 || (g.len > 0 && (!g.k || !g.v)) || g.row_stride < head_dim)
         return fail(DCC_ERR_INVALID_ARGUMENT, "attention_fwd: bad KV segment");
+      if (g.len == 0) continue;  // no keys: nothing is read
       mma = mma && aligned16(g.k) && aligned16(g.v) && g.row_stride % 8 == 0 &&
             g.k_head_stride % 8 == 0 && g.v_head_stride % 8 == 0;
     }

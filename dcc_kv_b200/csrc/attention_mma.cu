@@ -139,6 +139,25 @@ __global__ void __launch_bounds__(kThreads) attn_mma_bf16_kernel(const __grid_co
   const float sl2 = (float)prm.scale * kLog2e;
   float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
   const int64_t row_a = q0 + warp * 16 + (lane >> 2);  // this thread's rows: row_a, row_a + 8
+  if (p.o_init) {  // continue from (m = lse, l = 1, o = normalised partial); l summed over the quad
+    const __nv_bfloat16* oi = static_cast<const __nv_bfloat16*>(p.o_init) + h * p.o_head_stride;
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+      const int64_t row = row_a + 8 * r;
+      if (row >= p.Lq) continue;
+      const float lse0 = p.lse_init[h * p.lse_init_head_stride + row];
+      if (!(lse0 > -INFINITY)) continue;
+      m_run[r] = lse0 * kLog2e;
+      l_run[r] = (lane & 3) == 0 ? 1.f : 0.f;
+#pragma unroll
+      for (int nd = 0; nd < 16; ++nd) {
+        const int col = nd * 8 + 2 * (lane & 3);
+        const __nv_bfloat162 v2 = *reinterpret_cast<const __nv_bfloat162*>(oi + row * p.o_row_stride + col);
+        o[nd][2 * r] = __bfloat162float(v2.x);
+        o[nd][2 * r + 1] = __bfloat162float(v2.y);
+      }
+    }
+  }
 
   int buf = 0;
   while (cur.seg < p.n_seg) {

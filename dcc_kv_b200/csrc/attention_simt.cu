@@ -35,6 +35,19 @@ __global__ void __launch_bounds__(128) attn_simt_kernel(const __grid_constant__ 
     o[i] = Acc(0);
   }
   Acc m = NegInf<Acc>::v(), l = Acc(0);
+  if (p.o_init && valid) {  // continue from (m = lse, l = 1, o = normalised partial)
+    const float lse0 = p.lse_init[h * p.lse_init_head_stride + row];
+    if (lse0 > -INFINITY) {
+      m = Acc(lse0);
+      l = Acc(1);
+      const TIn* oi = static_cast<const TIn*>(p.o_init) + h * p.o_head_stride + row * p.o_row_stride;
+#pragma unroll
+      for (int i = 0; i < kMaxPer; ++i) {
+        const int c = part * per + i;
+        if (i < per && c < D) o[i] = to_acc<Acc, TIn>(oi[c]);
+      }
+    }
+  }
   const Acc scale = Acc(prm.scale);
   for (int sg = 0; sg < p.n_seg; ++sg) {
     const dcc_kv_segment& s = p.seg[sg];

@@ -52,6 +52,9 @@ struct Tc05Problem {
   int64_t Lq;
   int32_t n_seg, causal;
   int64_t causal_offset;
+  const void* o_init;  // optional initial state (o's strides), may alias o
+  const float* lse_init;
+  int64_t lse_init_head_stride;
   Tc05Seg seg[kTcMaxSeg];
 };
 
@@ -79,25 +82,30 @@ struct Smem {
   unsigned char k[2][kTileBytes];    // stages
   unsigned char v[2][kTileBytes];
   __align__(16) float bias[2][kKeys];
+  int64_t kend[kTcMaxSeg];  // segment ends clipped by the causal limit
   uint64_t bar_q, bar_k[2], bar_v[2], bar_bias[2], bar_empty[2], bar_s[2], bar_p[2], bar_o[2];
   uint32_t tmem;
 };
 
-struct Tile {
+// Walks this CTA's KV tiles in order (segments in order, 128 keys per tile,
+// empty segments skipped); the clipped segment ends live in shared memory.
+struct TileCursor {
   int seg;
   int64_t t0;
-  int64_t kend;
-};
-
-// The j-th KV tile of this CTA (segments in order, 128 keys per tile).
-__device__ __forceinline__ Tile tile_at(const Tc05Problem& p, const int64_t* kend, int j) {
-  for (int s = 0; s < p.n_seg; ++s) {
-    const int nt = (int)((kend[s] + kKeys - 1) / kKeys);
-    if (j < nt) return Tile{s, (int64_t)j * kKeys, kend[s]};
-    j -= nt;
+  __device__ __forceinline__ void start(const int64_t* kend, int n_seg) {
+    seg = 0;
+    t0 = 0;
+    while (seg < n_seg && kend[seg] <= 0) ++seg;
   }
-  return Tile{0, 0, 0};
-}
+  __device__ __forceinline__ void next(const int64_t* kend, int n_seg) {
+    t0 += kKeys;
+    if (t0 >= kend[seg]) {
+      t0 = 0;
+      ++seg;
+      while (seg < n_seg && kend[seg] <= 0) ++seg;
+    }
+  }
+};
 
 __device__ __forceinline__ uint64_t kdesc(const unsigned char* tile, int kk) {
   // K-major operand: 16-column step kk inside column block kk / 4
@@ -131,7 +139,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 using namespace fa;
 
 // ---- TMA producer (warp 8) --------------------------------------------------------
-__device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, const int64_t* kend, int n_tiles,
+__device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, int n_tiles,
                                               int64_t q0, int hA, int hB, int hk, int lane) {
   bool ok = true;
   if (lane == 0) {
@@ -143,13 +151,14 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
     tma_load_3d(sm.q[1] + 16384, &p.q, &sm.bar_q, 64, (int)q0, hB);
   }
   int issued = 0;
-  for (int j = 0; j < n_tiles; ++j) {
+  TileCursor t;
+  t.start(sm.kend, p.n_seg);
+  for (int j = 0; j < n_tiles; ++j, t.next(sm.kend, p.n_seg)) {
     const int st = j & 1;
     if (j >= 2 && !warp_wait(&sm.bar_empty[st], ((j >> 1) - 1) & 1)) {
       ok = false;
       break;
     }
-    const Tile t = tile_at(p, kend, j);
     const Tc05Seg& sg = p.seg[t.seg];
     if (lane == 0) {
       mbar_expect_tx(&sm.bar_k[st], kTileBytes);
@@ -164,7 +173,7 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
     for (int i = 0; i < 4; ++i) {
       const int c = lane * 4 + i;
       const int64_t key = t.t0 + c;
-      sm.bias[st][c] = (bg && key < t.kend) ? __ldg(bg + key) * 1.4426950408889634f : 0.f;  // log2 units
+      sm.bias[st][c] = (bg && key < sm.kend[t.seg]) ? __ldg(bg + key) * 1.4426950408889634f : 0.f;  // log2 units
     }
     mbar_arrive(&sm.bar_bias[st]);
     issued = j + 1;
@@ -184,7 +193,7 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, co
 // Issue order per tile j:  PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)  (S_A(0), S_B(0) first),
 // so head A's next scores are ready while head B's softmax still runs.  S(j+1)
 // overwrites P(j) in TMEM only after PV(j), issued earlier from this thread.
-__device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int lane) {
+__device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int lane, bool acc0) {
   const uint32_t id_s = idesc_bf16_f32(128, 128, 0, 0);
   const uint32_t id_pv = idesc_bf16_f32(128, 128, 0, 1);
   bool ok = warp_wait(&sm.bar_q, 0);
@@ -203,7 +212,7 @@ __device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int
       const uint32_t o_col = h ? kColOB : kColOA, p_col = h ? kColSB : kColSA;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        umma_ts(tm + o_col, tm + p_col + kk * 8, vdesc(sm.v[st], kk), id_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        umma_ts(tm + o_col, tm + p_col + kk * 8, vdesc(sm.v[st], kk), id_pv, (acc0 || j > 0 || kk > 0) ? 1u : 0u);
       umma_commit(&sm.bar_o[h]);
     }
     __syncwarp();
@@ -251,18 +260,52 @@ __device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int
 
 // ---- softmax + epilogue (warps 0-3: head A, 4-7: head B) ------------------------
 __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Problem& p, Smem& sm,
-                                             const int64_t* kend, int n_tiles, int64_t q0, int hA, int hB,
+                                             int n_tiles, int64_t q0, int hA, int hB,
                                              uint32_t tm, int warp, int lane) {
   const int role = warp >> 2;
   const int row = (warp & 3) * 32 + lane;
   const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
   const uint32_t s_col = role ? kColSB : kColSA, o_col = role ? kColOB : kColOA;
   const int64_t q_row = q0 + row;
+  const int h = role ? hB : hA;
   float m_use = -INFINITY, l = 0.f;
   bool ok = true;
-  for (int j = 0; j < n_tiles; ++j) {
+  // Optional initial state (m = lse_init, l = 1, O = o_init): O goes to TMEM
+  // before the first P hand-off (whose tcgen05.wait::st covers these stores);
+  // rows past Lq or without keys so far start empty.
+  const bool init = p.o_init != nullptr;
+  if (init) {
+    const bool real = q_row < p.Lq;
+    const float lse0 = real ? p.lse_init[h * p.lse_init_head_stride + q_row] : -INFINITY;
+    const bool have = lse0 > -INFINITY;
+    if (have) {
+      m_use = lse0 * 1.4426950408889634f;
+      l = 1.f;
+    }
+    const uint4* oi = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(p.o_init) +
+                                                     h * p.o_head_stride + (real ? q_row : 0) * p.o_row_stride);
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t r[32];
+#pragma unroll
+      for (int v = 0; v < 4; ++v) {
+        const uint4 w = have ? oi[4 * c + v] : make_uint4(0u, 0u, 0u, 0u);
+        const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {  // bf16 pair -> two fp32 (a bf16 is the top half of its fp32)
+          r[8 * v + 2 * i] = ws[i] << 16;
+          r[8 * v + 2 * i + 1] = ws[i] & 0xffff0000u;
+        }
+      }
+      tmem_st32(tm + lane_off + o_col + 32 * c, r);
+    }
+    tmem_wait_st();
+  }
+  TileCursor t;
+  t.start(sm.kend, p.n_seg);
+  for (int j = 0; j < n_tiles; ++j, t.next(sm.kend, p.n_seg)) {
     const int st = j & 1;
-    const Tile t = tile_at(p, kend, j);
+    const int64_t t_end = sm.kend[t.seg];
     const bool causal = p.causal && t.seg == 0;
     if (!warp_wait(&sm.bar_s[role], j & 1)) {
       ok = false;
@@ -278,8 +321,8 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
       break;
     }
     // visible keys of this row in the tile: [t0, t0 + nvis)
-    const int64_t lim = causal ? q_row + p.causal_offset : t.kend - 1;  // last visible key
-    const int64_t lim2 = lim < t.kend - 1 ? lim : t.kend - 1;
+    const int64_t lim = causal ? q_row + p.causal_offset : t_end - 1;  // last visible key
+    const int64_t lim2 = lim < t_end - 1 ? lim : t_end - 1;
     const int nvis = (int)(lim2 - t.t0 + 1 < 0 ? 0 : (lim2 - t.t0 + 1 > 128 ? 128 : lim2 - t.t0 + 1));
     const bool full = __all_sync(0xffffffffu, nvis == 128) != 0;
     const bool biased = p.seg[t.seg].bias != nullptr;
@@ -320,8 +363,8 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     const bool need = mt > m_use + 8.f;
     if (__any_sync(0xffffffffu, need)) {
       const float corr = !need ? 1.f : (m_use == -INFINITY ? 0.f : exp2f(m_use - mt));
-      if (j > 0) {
-        if (!warp_wait(&sm.bar_o[role], (j - 1) & 1)) {
+      if (j > 0 || init) {
+        if (j > 0 && !warp_wait(&sm.bar_o[role], (j - 1) & 1)) {
           ok = false;
           break;
         }
@@ -366,7 +409,6 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     mbar_arrive(&sm.bar_p[role]);
   }
   if (!ok) atomicOr(&g_attn_error, 4u);
-  const int h = role ? hB : hA;
   if (ok && n_tiles > 0 && !warp_wait(&sm.bar_o[role], (n_tiles - 1) & 1)) {
     ok = false;
     atomicOr(&g_attn_error, 8u);
@@ -379,7 +421,7 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
 #pragma unroll 1
   for (int c = 0; c < 4; ++c) {
     uint32_t r[32];
-    if (n_tiles > 0) {
+    if (n_tiles > 0 || init) {
       tmem_ld32(tm + lane_off + o_col + 32 * c, r);
       tmem_wait_ld();
     } else {
@@ -413,7 +455,6 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_con
   const int hA = 2 * blockIdx.y, hB = hA + 1, hk = hA / b.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  int64_t kend[kTcMaxSeg];
   int n_tiles = 0;
   for (int s = 0; s < kTcMaxSeg; ++s) {
     int64_t e = s < p.n_seg ? p.seg[s].len : 0;
@@ -421,8 +462,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_con
       const int64_t last = (q0 + kRows - 1 < p.Lq - 1 ? q0 + kRows - 1 : p.Lq - 1) + p.causal_offset + 1;
       e = e < last ? e : last;
     }
-    kend[s] = e > 0 ? e : 0;
-    n_tiles += (int)((kend[s] + kKeys - 1) / kKeys);
+    e = e > 0 ? e : 0;
+    if (threadIdx.x == 0) sm.kend[s] = e;
+    n_tiles += (int)((e + kKeys - 1) / kKeys);
   }
 
   if (threadIdx.x == 0) {
@@ -448,11 +490,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_con
   const uint32_t tm = sm.tmem;
   if (warp >= 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsOther));
-    if (warp == 8) producer_role(p, sm, kend, n_tiles, q0, hA, hB, hk, lane);
-    else if (warp == 9) mma_role(sm, n_tiles, tm, lane);
+    if (warp == 8) producer_role(p, sm, n_tiles, q0, hA, hB, hk, lane);
+    else if (warp == 9) mma_role(sm, n_tiles, tm, lane, p.o_init != nullptr);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsSoftmax));
-    softmax_role(b, p, sm, kend, n_tiles, q0, hA, hB, tm, warp, lane);
+    softmax_role(b, p, sm, n_tiles, q0, hA, hB, tm, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -503,7 +545,8 @@ int launch_attn_tc05(const dcc_attn_problem* probs, int n, const AttnParams& prm
     const dcc_attn_problem& q = probs[i];
     Tc05Problem& t = b.p[b.n];
     t = Tc05Problem{};
-    DCC_CHECK(make_tmap_bf16_3d(&t.q, q.q, 128, q.Lq, prm.n_q_heads, q.q_row_stride, q.q_head_stride, 128));
+    if (q.Lq > 0)  // an empty problem launches no CTA and needs no map
+      DCC_CHECK(make_tmap_bf16_3d(&t.q, q.q, 128, q.Lq, prm.n_q_heads, q.q_row_stride, q.q_head_stride, 128));
     t.o = q.o;
     t.lse = q.lse;
     t.o_head_stride = q.o_head_stride;
@@ -513,11 +556,16 @@ int launch_attn_tc05(const dcc_attn_problem* probs, int n, const AttnParams& prm
     t.n_seg = q.n_seg;
     t.causal = q.causal;
     t.causal_offset = q.causal_offset;
+    t.o_init = q.o_init;
+    t.lse_init = q.lse_init;
+    t.lse_init_head_stride = q.lse_init_head_stride;
     for (int s = 0; s < q.n_seg; ++s) {
       const dcc_kv_segment& g = q.seg[s];
       Tc05Seg& ts = t.seg[s];
-      DCC_CHECK(make_tmap_bf16_3d(&ts.k, g.k, 128, g.len, prm.n_kv_heads, g.row_stride, g.k_head_stride, 128));
-      DCC_CHECK(make_tmap_bf16_3d(&ts.v, g.v, 128, g.len, prm.n_kv_heads, g.row_stride, g.v_head_stride, 128));
+      if (g.len > 0) {  // an empty segment contributes no tile and needs no map
+        DCC_CHECK(make_tmap_bf16_3d(&ts.k, g.k, 128, g.len, prm.n_kv_heads, g.row_stride, g.k_head_stride, 128));
+        DCC_CHECK(make_tmap_bf16_3d(&ts.v, g.v, 128, g.len, prm.n_kv_heads, g.row_stride, g.v_head_stride, 128));
+      }
       ts.bias = g.bias;
       ts.bias_head_stride = g.bias_head_stride;
       ts.len = g.len;

@@ -50,7 +50,17 @@ const char* dcc_status_string(int status) {
 
 const char* dcc_last_error(void) { return dcc::g_last_error.c_str(); }
 
-int dcc_version(void) { return 1; }
+int dcc_version(void) { return 2; }
+
+size_t dcc_struct_size(const char* name) {
+  if (!name) return 0;
+  const std::string n(name);
+  if (n == "dcc_query_set") return sizeof(dcc_query_set);
+  if (n == "dcc_build_problem") return sizeof(dcc_build_problem);
+  if (n == "dcc_kv_segment") return sizeof(dcc_kv_segment);
+  if (n == "dcc_attn_problem") return sizeof(dcc_attn_problem);
+  return 0;
+}
 
 // torch's CPU generator is mt19937 seeded with the low 32 bits of the seed
 // (the standard init_genrand); randint(lo, hi) for a range below 2^32 is

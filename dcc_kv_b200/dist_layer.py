@@ -17,8 +17,9 @@ balances across ranks).  One forward on every rank:
   3. local causal attention on the main stream from the start, overlapped
      with (0)-(2);
   4. compact attention with logit bias, one KV segment per source edge,
-     read in place from the receive / local buffers;
-  5. online-softmax merge into the local output.
+     read in place from the receive / local buffers, continuing each
+     block's online softmax from the local (O, LSE) in place -- the merge
+     (online_softmax.py:92-111) happens inside that launch.
 
 ``DistPlan`` is the pure host-side routing (offsets and split sizes),
 identical on every rank and testable without a GPU.
@@ -35,7 +36,6 @@ from . import _lib as L
 from .attention import attn_problem, kv_segment, run_attention
 from .compact_kv import build_launch_count, build_problem, run_build_problems
 from .layer import Budgets, budget_table
-from .online_softmax import merge_lse
 from .representative_query import query_set, select_query_sets
 from .var_len_msg import EdgeLayout
 
@@ -146,8 +146,6 @@ class DistributedDccKvLayer:
                         for e, loc in self.plan.send_offsets(self.rank).items()}
         self.o_loc = torch.empty(self.n_local, n_q_heads, block_len, head_dim, dtype=dtype, device=dev)
         self.lse_loc = torch.empty(self.n_local, n_q_heads, block_len, dtype=torch.float32, device=dev)
-        self.o_c = torch.empty_like(self.o_loc)
-        self.lse_c = torch.empty_like(self.lse_loc)
         # pooling, the gather, the builds and the exchange run on a high-priority
         # side stream, so their kernels are dispatched ahead of the local
         # attention that fills the GPU meanwhile on the main stream
@@ -183,7 +181,9 @@ class DistributedDccKvLayer:
         self.local_problems = [attn_problem(q[li], self.o_loc[li], self.lse_loc[li], [kv_segment(k[li], v[li])],
                                             causal=True) for li in range(self.n_local)]
         recv_off = self.plan.recv_offsets(self.rank)
-        self.compact_problems, self.merge_rows = [], []
+        # the compact blocks continue each local block's online softmax from
+        # its (O, LSE), in place: the merge needs no separate pass
+        self.compact_problems = []
         for li, r in enumerate(self.local_blocks):
             segs = []
             for s in range(r):
@@ -191,8 +191,8 @@ class DistributedDccKvLayer:
                 ko, vo, bo = self.plan.layout[(s, r)].views(self.bufs[buf], off, self.dtype)
                 segs.append(kv_segment(ko, vo, bo))
             if segs:
-                self.compact_problems.append(attn_problem(q[li], self.o_c[li], self.lse_c[li], segs))
-                self.merge_rows.append(li)
+                self.compact_problems.append(attn_problem(q[li], self.o_loc[li], None, segs,
+                                                          o_init=self.o_loc[li], lse_init=self.lse_loc[li]))
         self._bound = key
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
@@ -260,11 +260,8 @@ class DistributedDccKvLayer:
                 self._attention([self.local_problems[li]])
         main.wait_stream(side)
         run_attention(self.compact_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code, dev)
-        for li in range(self.n_local):
-            if li in self.merge_rows:
-                merge_lse([self.o_loc[li], self.o_c[li]], [self.lse_loc[li], self.lse_c[li]], out=self.o_loc[li],
-                          want_lse=False)
-            if merged is not None:
+        if merged is not None:
+            for li in range(self.n_local):
                 merged[li].record(main)
 
     def _forward_host(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out) -> torch.Tensor:
@@ -332,4 +329,4 @@ class DistributedDccKvLayer:
         sets = len(self.sets)
         pool = 0 if sets == 0 else 2 * -(-sets // 64)
         return (pool + build_launch_count(len(self.build), self.code, self.d) + -(-len(self.local_problems) // 8)
-                + -(-len(self.compact_problems) // 8) + len(self.merge_rows))
+                + -(-len(self.compact_problems) // 8))

@@ -43,7 +43,12 @@ enum { DCC_F32 = 0, DCC_BF16 = 1, DCC_F64 = 2 };
 
 const char* dcc_status_string(int status);
 const char* dcc_last_error(void);
+/* ABI version: 2 added the initial state of dcc_attn_problem. */
 int dcc_version(void);
+/* sizeof of an ABI struct by its name ("dcc_query_set", "dcc_build_problem",
+ * "dcc_kv_segment", "dcc_attn_problem"), 0 for an unknown name -- lets a
+ * foreign-function binding check its struct layouts. */
+size_t dcc_struct_size(const char* name);
 
 /* ---- host-side random draws (torch.Generator-compatible mt19937) ---------
  * Replaces representative_query.py:10-31 (rademacher_projection): writes
@@ -223,6 +228,14 @@ typedef struct dcc_attn_problem {
   int32_t causal;
   int64_t causal_offset;
   dcc_kv_segment seg[DCC_MAX_SEGMENTS];
+  /* Optional initial online-softmax state (NULL: none): a normalised partial
+   * output o_init (o's shape and strides, may alias o) with its log-sum-exp
+   * lse_init ([n_q_heads, Lq], may alias lse).  The rows continue from
+   * (m = lse_init, l = 1, o = o_init), so the result is the merge of that
+   * state with the attention over the segments (online_softmax.py:92-111). */
+  const void* o_init;
+  const float* lse_init;
+  int64_t lse_init_head_stride;
 } dcc_attn_problem;
 
 int dcc_attention_fwd(const dcc_attn_problem* problems, int n_problems, int n_q_heads,

@@ -39,7 +39,14 @@ def test_status_strings():
     lib = L.lib()
     assert lib.dcc_status_string(0) == b"ok"
     assert lib.dcc_status_string(L.DCC_ERR_WORKSPACE) == b"workspace too small"
-    assert lib.dcc_version() >= 1
+    assert lib.dcc_version() >= 2
+
+
+def test_ctypes_struct_layouts_match_the_library():
+    lib = L.lib()
+    for cls in (L.dcc_query_set, L.dcc_build_problem, L.dcc_kv_segment, L.dcc_attn_problem):
+        assert lib.dcc_struct_size(cls.__name__.encode()) == C.sizeof(cls), cls.__name__
+    assert lib.dcc_struct_size(b"no_such_struct") == 0
 
 
 @pytest.mark.parametrize("seed,dp,d", [(42, 32, 128), (0, 8, 32), (12345, 16, 64), (7, 5, 7)])

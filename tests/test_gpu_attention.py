@@ -135,3 +135,47 @@ def test_attention_small_head_dim_f32():
 ])
 def test_attention_tc05_shapes_bf16(hq, hkv, lq, segs, causal):
     _attn_case(torch.bfloat16, hq, hkv, lq, 128, segs, causal, hq * 7 + lq)
+
+
+@pytest.mark.parametrize("dtype,hq,hkv,d", [
+    (torch.bfloat16, 8, 2, 128),   # tcgen05 kernel
+    (torch.bfloat16, 3, 3, 128),   # odd GQA group: the mma.sync kernel
+    (torch.float32, 4, 2, 64),     # FP64-accumulating CUDA-core kernel
+])
+def test_attention_continues_from_initial_state(dtype, hq, hkv, d):
+    """Two launches -- causal local keys, then biased compact keys starting
+    from the first launch's (O, LSE), in place -- equal the one-pass merge;
+    an empty second segment passes the state through."""
+    g = torch.Generator().manual_seed(hq * 31 + d)
+    lq = 300
+    q = torch.randn(hq, lq, d, generator=g, dtype=torch.float64)
+    k1, v1 = (torch.randn(hkv, lq, d, generator=g, dtype=torch.float64) for _ in range(2))
+    k2, v2 = (torch.randn(hkv, 200, d, generator=g, dtype=torch.float64) for _ in range(2))
+    b2 = torch.randn(hkv, 200, generator=g, dtype=torch.float64) * 3 + 4  # compact logits above the local ones
+    cast = lambda t: t.to(dtype).to(dev())
+    o1, l1 = dk.attention(cast(q), [(cast(k1), cast(v1), None)], causal=True)
+    o2, l2 = dk.attention(cast(q), [(cast(k2), cast(v2), b2.float().to(dev()))], init=(o1, l1))
+    o3, l3 = dk.attention(cast(q), [(cast(k2[:, :0]), cast(v2[:, :0]), None)], init=(o1, l1))
+    torch.cuda.synchronize()
+    assert L.lib().dcc_device_error_status(1) == 0, "a bounded device wait expired"
+    tol = 2e-2 if dtype == torch.bfloat16 else 1e-4
+    grp = hq // hkv
+    qd = q.to(dtype).double().numpy()
+    for h in range(hq):
+        kk1, vv1 = (x[h // grp].to(dtype).double().numpy() for x in (k1, v1))
+        kk2, vv2 = (x[h // grp].to(dtype).double().numpy() for x in (k2, v2))
+        p1 = orc.attention_partial(qd[h], kk1, vv1, positions=np.arange(lq))
+        p2 = orc.attention_partial(qd[h], kk2, vv2, bias=b2[h // grp].float().double().numpy())
+        want_o, want_l = orc.merge_lse([p1[0], p2[0]], [p1[1], p2[1]])
+        assert rel_err(np64(o2[h]), want_o) < tol, h
+        assert rel_err(np64(l2[h]), want_l) < (1e-2 if dtype == torch.bfloat16 else 1e-5), h
+        assert rel_err(np64(o3[h]), p1[0]) < tol, h
+        assert rel_err(np64(l3[h]), p1[1]) < (1e-2 if dtype == torch.bfloat16 else 1e-5), h
+    # in place: the initial state aliasing the outputs
+    from dcc_kv_b200.attention import attn_problem, kv_segment, run_attention
+    o_in, l_in = o1.clone(), l1.clone()
+    qc, kc, vc, bc = cast(q), cast(k2), cast(v2), b2.float().to(dev())
+    prob = attn_problem(qc, o_in, l_in, [kv_segment(kc, vc, bc)], o_init=o_in, lse_init=l_in)
+    run_attention([prob], hq, hkv, d, 1.0 / d ** 0.5, L.dtype_code(qc), dev())
+    torch.cuda.synchronize()
+    assert torch.equal(o_in, o2) and torch.equal(l_in, l2)

@@ -23,13 +23,15 @@ from gpu_util import assert_no_device_timeouts, dev, golden, np64, rel_err, to_g
 pytestmark = pytest.mark.gpu
 
 
-def test_small_layer_golden_f32():
+@pytest.mark.parametrize("schedule", ["batched", "pipelined"])
+def test_small_layer_golden_f32(schedule):
     f = golden("layer_small.npz")
     nb, hq, L, d = f["Q"].shape
     hkv = f["K"].shape[1]
     budgets = {(int(s), int(r)): int(b) for s, r, b in f["budgets"]}
     layer = dk.DccKvSyncLayer(nb, L, hq, hkv, d, budgets, int(f["window"]), int(f["M"]), int(f["dp"]),
                               dtype=torch.float32)
+    layer.schedule = schedule
     out = layer(to_gpu(f["Q"], torch.float32), to_gpu(f["K"], torch.float32), to_gpu(f["V"], torch.float32))
     torch.cuda.synchronize()
     assert rel_err(np64(out), f["out"]) < 1e-4
@@ -67,12 +69,14 @@ def _oracle_layer(q, k, v, budgets, window, M, dp, rows=None):
     return orc.layer_forward(qb, kb, vb, budgets, window, M, dp, rows=rows)
 
 
-def test_layer_bf16_small():
+@pytest.mark.parametrize("schedule", ["batched", "pipelined"])
+def test_layer_bf16_small(schedule):
     from dcc_kv_b200.workloads import layer_inputs
     nb, L, hq, hkv, d = 4, 512, 8, 2, 128
     q, k, v = layer_inputs(nb, L, hq, hkv, d, device="cpu", first_seed=7)
     budgets = {(s, r): [64, 96, 128][(s + 2 * r) % 3] for r in range(nb) for s in range(r)}
     layer = dk.DccKvSyncLayer(nb, L, hq, hkv, d, budgets, window=128)
+    layer.schedule = schedule
     out = layer(q.to(dev()), k.to(dev()), v.to(dev()))
     torch.cuda.synchronize()
     assert_no_device_timeouts()
