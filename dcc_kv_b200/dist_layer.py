@@ -152,38 +152,56 @@ class DistributedDccKvLayer:
         lo, hi = torch.cuda.Stream.priority_range()
         self.comm_stream = torch.cuda.Stream(device=dev, priority=hi)
         self._bound = None
+        self._bindings = {}
+        self._ws, self._ws_bytes = None, 0
         self.timing_events = None
         self.timing_index = 0
 
     def _bind(self, q, k, v):
+        """Point the kernel descriptors at q, k, v; descriptor sets are cached
+        per input buffers (the host-buffer path alternates between two device
+        staging sets) and the build workspace only grows."""
         key = (q.data_ptr(), k.data_ptr(), v.data_ptr())
         if self._bound == key:
             return
+        bound = self._bindings.get(key)
+        if bound is None:
+            bound = self._make_binding(q, k, v)
+            if len(self._bindings) >= 4:
+                self._bindings.pop(next(iter(self._bindings)))
+            self._bindings[key] = bound
+        self.sets, self.build, self.local_problems, self.compact_problems, need = bound
+        if need > self._ws_bytes:
+            # the workspace may still be in use by the side stream
+            torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
+            self._ws, self._ws_bytes = L.workspace(need, self.device), need
+        self._bound = key
+
+    def _make_binding(self, q, k, v):
         g = self.qgroup
-        self.sets = [query_set(q[li, h * g], self.repr_local[li, h], self.repr_idx[li, h], n_seg=g,
+        sets = [query_set(q[li, h * g], self.repr_local[li, h], self.repr_idx[li, h], n_seg=g,
                                seg_rows=self.window, seg_stride=q.stride(1), row_stride=q.stride(2))
-                     for li, b in enumerate(self.local_blocks) if b > 0 for h in range(self.hkv)]
+                for li, b in enumerate(self.local_blocks) if b > 0 for h in range(self.hkv)]
         send_off = self.plan.send_offsets(self.rank)
-        self.build = []
+        build = []
         for (s, r), (buf, off) in sorted(send_off.items()):
             lay = self.plan.layout[(s, r)]
             ko, vo, bo = lay.views(self.bufs[buf], off, self.dtype)
             rep = self.repr_all[self.plan.owner(r), self.plan.local_index(r)]
             ls = self.plan.local_index(s)
             for h in range(self.hkv):
-                self.build.append(build_problem(k[ls, h], v[ls, h], rep[h], self.plan.budgets[(s, r)], ko[h], vo[h],
-                                                bo[h], self.sel_idx[(s, r)][h], num_repr=self.m_eff))
-        self._ws = None
-        if self.build:
-            arr = (L.dcc_build_problem * len(self.build))(*self.build)
-            need = L.lib().dcc_build_compact_kv_workspace_bytes(arr, len(self.build), self.d, self.d, self.code)
-            self._ws = L.workspace(need, self.device)
-        self.local_problems = [attn_problem(q[li], self.o_loc[li], self.lse_loc[li], [kv_segment(k[li], v[li])],
-                                            causal=True) for li in range(self.n_local)]
+                build.append(build_problem(k[ls, h], v[ls, h], rep[h], self.plan.budgets[(s, r)], ko[h], vo[h],
+                                           bo[h], self.sel_idx[(s, r)][h], num_repr=self.m_eff))
+        need = 0
+        if build:
+            arr = (L.dcc_build_problem * len(build))(*build)
+            need = L.lib().dcc_build_compact_kv_workspace_bytes(arr, len(build), self.d, self.d, self.code)
+        local_problems = [attn_problem(q[li], self.o_loc[li], self.lse_loc[li], [kv_segment(k[li], v[li])],
+                                       causal=True) for li in range(self.n_local)]
         recv_off = self.plan.recv_offsets(self.rank)
         # the compact blocks continue each local block's online softmax from
         # its (O, LSE), in place: the merge needs no separate pass
-        self.compact_problems = []
+        compact_problems = []
         for li, r in enumerate(self.local_blocks):
             segs = []
             for s in range(r):
@@ -191,9 +209,9 @@ class DistributedDccKvLayer:
                 ko, vo, bo = self.plan.layout[(s, r)].views(self.bufs[buf], off, self.dtype)
                 segs.append(kv_segment(ko, vo, bo))
             if segs:
-                self.compact_problems.append(attn_problem(q[li], self.o_loc[li], None, segs,
-                                                          o_init=self.o_loc[li], lse_init=self.lse_loc[li]))
-        self._bound = key
+                compact_problems.append(attn_problem(q[li], self.o_loc[li], None, segs,
+                                                     o_init=self.o_loc[li], lse_init=self.lse_loc[li]))
+        return sets, build, local_problems, compact_problems, need
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
         """Local blocks q [n_local, H_q, L, d], k / v [n_local, H_kv, L, d] ->
@@ -279,27 +297,32 @@ class DistributedDccKvLayer:
             raise ValueError(f"out must be a contiguous CPU {self.dtype} tensor of shape {exp_q}")
         dev = self.device
         if getattr(self, "_staging", None) is None:
-            self._staging = (torch.empty_like(q, device=dev), torch.empty_like(k, device=dev),
-                             torch.empty_like(v, device=dev))
+            # two device staging sets, alternated by consecutive calls, so the
+            # copy-in of one call overlaps the compute of the previous one
+            self._staging = [(torch.empty_like(q, device=dev), torch.empty_like(k, device=dev),
+                              torch.empty_like(v, device=dev)) for _ in range(2)]
+            self._staging_done = [None, None]
+            self._host_calls = 0
             self._h2d = torch.cuda.Stream(device=dev)
             self._d2h = torch.cuda.Stream(device=dev)
             self._ev_win, self._ev_kv = torch.cuda.Event(), torch.cuda.Event()
             self._ev_q = [torch.cuda.Event() for _ in range(self.n_local)]
             self._ev_merged = [torch.cuda.Event() for _ in range(self.n_local)]
             self._ev_drained = [torch.cuda.Event() for _ in range(self.n_local)]
-            self._ev_done = None
-        dq, dk_, dv = self._staging
+        i = self._host_calls % 2
+        self._host_calls += 1
+        dq, dk_, dv = self._staging[i]
         self._bind(dq, dk_, dv)
         main = torch.cuda.current_stream(dev)
         h2d, d2h = self._h2d, self._d2h
         W = self.window
-        # the previous call's kernels must be done with the staging buffers,
-        # and its copy-out with the output buffers
-        if self._ev_done is None:
-            self._ev_done = torch.cuda.Event()
+        # the kernels of the call before the previous one must be done with
+        # this staging set, and the previous call's copy-out with the outputs
+        if self._staging_done[i] is None:
             h2d.wait_stream(main)
         else:
-            h2d.wait_event(self._ev_done)
+            h2d.wait_event(self._staging_done[i])
+        self._staging_done[i] = torch.cuda.Event()
         for li in range(self.n_local):
             main.wait_event(self._ev_drained[li])
         with torch.cuda.stream(h2d):
@@ -316,7 +339,7 @@ class DistributedDccKvLayer:
                         dq[li, h, W:].copy_(q[li, h, W:], non_blocking=True)
                 self._ev_q[li].record(h2d)
         self._run(self._ev_win, self._ev_kv, self._ev_q, self._ev_merged)
-        self._ev_done.record(main)
+        self._staging_done[i].record(main)
         with torch.cuda.stream(d2h):
             for li in range(self.n_local):
                 d2h.wait_event(self._ev_merged[li])

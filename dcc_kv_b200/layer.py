@@ -85,9 +85,13 @@ class DccKvSyncLayer:
         self.ci = [torch.empty(n_kv_heads, t, dtype=torch.int64, device=dev) for t in self.total]
         self.out = torch.empty(n_blocks, n_q_heads, block_len, d, dtype=dtype, device=dev)
         self._bound = None
-        self._ws = None
+        self._bindings: Dict[Tuple[int, int, int, int], tuple] = {}
+        self._ws, self._ws_bytes = None, 0
+        self._ws2, self._ws2_bytes = None, 0
         self._host_out = None
         self._staging = None
+        self._host_stream = None
+        self._last_call_host = False
         self._streams = None
         # "batched" (default): pooling, the builds (two halves on two streams),
         # then one attention launch; "pipelined": builds on a side stream
@@ -101,41 +105,63 @@ class DccKvSyncLayer:
         self.timing_index = 0
 
     # -- descriptors (rebuilt only when the input tensors change) ------------
-    def _bind(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> None:
-        key = (q.data_ptr(), k.data_ptr(), v.data_ptr())
+    def _bind(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: Optional[torch.Tensor] = None) -> None:
+        """Point the kernel descriptors at q, k, v and the device output
+        ``out`` (default: the internal buffer ``self.out``).  Descriptor sets
+        are cached per buffers (the host-buffer path alternates between two
+        device staging sets), and the build workspaces are shared: they only
+        grow."""
+        out = self.out if out is None else out
+        key = (q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr())
         if self._bound == key:
             return
-        if self._streams is not None:
-            # the workspace below may still be in use by the side stream
-            torch.cuda.current_stream(self.device).wait_stream(self._streams[1])
+        bound = self._bindings.get(key)
+        if bound is None:
+            bound = self._make_binding(q, k, v, out)
+            if len(self._bindings) >= 4:
+                self._bindings.pop(next(iter(self._bindings)))
+            self._bindings[key] = bound
+        (self.sets, self.sets_of, self.build, self.build_of, self.build_halves, self.attn_problems,
+         (need, need2)) = bound
+        if need > self._ws_bytes or need2 > self._ws2_bytes:
+            if self._streams is not None:
+                # the workspaces may still be in use by the side stream
+                torch.cuda.current_stream(self.device).wait_stream(self._streams[1])
+            if need > self._ws_bytes:
+                self._ws, self._ws_bytes = L.workspace(need, self.device), need
+            if need2 > self._ws2_bytes:
+                self._ws2, self._ws2_bytes = L.workspace(need2, self.device), need2
+        self._bound = key
+
+    def _make_binding(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor):
         g = self.group
-        self.sets = []
+        sets = []
         # per destination block r: its query sets and the edges s -> r, as
         # slices of the batched lists (the host-buffer path runs them block by block)
-        self.sets_of = [slice(0, 0)]
-        self.build_of = [slice(0, 0)]
+        sets_of = [slice(0, 0)]
+        build_of = [slice(0, 0)]
         for r in range(1, self.nb):
-            self.sets_of.append(slice(len(self.sets), len(self.sets) + self.hkv))
+            sets_of.append(slice(len(sets), len(sets) + self.hkv))
             for h in range(self.hkv):
-                self.sets.append(query_set(q[r, h * g], self.repr[r, h], self.repr_idx[r, h], n_seg=g,
-                                           seg_rows=self.window, seg_stride=q.stride(1), row_stride=q.stride(2)))
-        self.build = []
+                sets.append(query_set(q[r, h * g], self.repr[r, h], self.repr_idx[r, h], n_seg=g,
+                                      seg_rows=self.window, seg_stride=q.stride(1), row_stride=q.stride(2)))
+        build = []
         for r in range(1, self.nb):
-            self.build_of.append(slice(len(self.build), len(self.build) + r * self.hkv))
+            build_of.append(slice(len(build), len(build) + r * self.hkv))
             for s in range(r):
                 b = self.budgets[(s, r)]
                 bp = min(b, self.L)
                 o = self.offsets[(s, r)]
                 for h in range(self.hkv):
-                    self.build.append(build_problem(
+                    build.append(build_problem(
                         k[s, h], v[s, h], self.repr[r, h], b, self.ck[r][h, o:o + bp], self.cv[r][h, o:o + bp],
                         self.cb[r][h, o:o + bp], self.ci[r][h, o:o + bp], num_repr=self.m_eff))
         # batched schedule: the edges split in two halves (by destination block)
         # that run on two streams, so the latency-bound calibration launches of
         # one half overlap those of the other
-        half = len(self.build) // 2
-        cut = min((sl.stop for sl in self.build_of[1:]), key=lambda e: abs(e - half), default=0)
-        self.build_halves = [slice(0, cut), slice(cut, len(self.build))]
+        half = len(build) // 2
+        cut = min((sl.stop for sl in build_of[1:]), key=lambda e: abs(e - half), default=0)
+        build_halves = [slice(0, cut), slice(cut, len(build))]
 
         def ws_bytes(probs):
             if not probs:
@@ -143,22 +169,18 @@ class DccKvSyncLayer:
             arr = (L.dcc_build_problem * len(probs))(*probs)
             return L.lib().dcc_build_compact_kv_workspace_bytes(arr, len(probs), self.d, self.d, self.code)
 
-        need = max([ws_bytes(self.build[part]) for part in
-                    [slice(0, len(self.build)), self.build_halves[0]] + self.build_of[1:]] + [0])
-        if need:
-            self._ws = L.workspace(need, self.device)
-        need2 = ws_bytes(self.build[self.build_halves[1]])
-        self._ws2 = L.workspace(need2, self.device) if need2 else None
+        need = max([ws_bytes(build[part]) for part in [slice(0, len(build)), build_halves[0]] + build_of[1:]] + [0])
+        need2 = ws_bytes(build[build_halves[1]])
         # one attention problem per block: its causal local segment, then (for r >= 1)
         # the concatenated compact blocks with their logit bias -- the online softmax
         # runs over both in one pass, so no separate merge is needed
-        self.attn_problems = []
+        attn_problems = []
         for b in range(self.nb):
             segs = [kv_segment(k[b], v[b])]
             if b > 0 and self.total[b] > 0:
                 segs.append(kv_segment(self.ck[b], self.cv[b], self.cb[b]))
-            self.attn_problems.append(attn_problem(q[b], self.out[b], None, segs, causal=True))
-        self._bound = key
+            attn_problems.append(attn_problem(q[b], out[b], None, segs, causal=True))
+        return sets, sets_of, build, build_of, build_halves, attn_problems, (need, need2)
 
     def check_inputs(self, q, k, v):
         L.require_cuda(q, k, v)
@@ -182,6 +204,10 @@ class DccKvSyncLayer:
         if not q.is_cuda:
             return self._forward_host(q, k, v, out)
         self.check_inputs(q, k, v)
+        if self._host_stream is not None and self._last_call_host:
+            # the internal buffers were last used by the host-buffer path's stream
+            torch.cuda.current_stream(self.device).wait_stream(self._host_stream)
+        self._last_call_host = False
         self._bind(q, k, v)
         if self.schedule == "batched":
             self._forward_batched()
@@ -230,22 +256,27 @@ class DccKvSyncLayer:
             # of the attention CTAs that fill the GPU), copy-out
             self._streams = tuple(torch.cuda.Stream(device=dev, priority=p) for p in (0, hi, 0))
             self._events = [[torch.cuda.Event() for _ in range(self.nb)] for _ in range(4)]
-            self._compute_done = torch.cuda.Event()
 
-    def _run_blocks(self, pool_all: bool, copy_in=None, copy_out=None) -> None:
+    def _run_blocks(self, pool_all: bool, copy_in=None, copy_out=None, inputs_free=None,
+                    inputs_done=None, drained=None) -> None:
         """Per-block schedule.  Side stream (high priority): pooling, then for
         b = 1 .. nb-1 the builds s -> b; current stream: attention of block b
         as soon as its compacts are built (block 0 needs none and starts at
         once), so the latency-bound pooling / build kernels share the GPU
         with attention instead of running before it.  ``copy_in(b)`` /
-        ``copy_out(b)``, when given, run on the copy-in / copy-out streams."""
+        ``copy_out(b)``, when given, run on the copy-in / copy-out streams;
+        the copy-in waits for ``inputs_free`` (the last compute that read the
+        staging buffers), ``inputs_done`` is recorded once this call's
+        compute no longer reads them, and ``drained[b]`` (waited before block
+        b's attention overwrites its output, recorded after its copy-out)
+        belongs to the device output buffer in use."""
         dev = self.device
         h2d, side, d2h = self._streams
-        copied, built, attended, drained = self._events
+        copied, built, attended = self._events[:3]
         main = torch.cuda.current_stream(dev)
         if copy_in is not None:
-            # the previous call's kernels must be done reading the staging buffers
-            h2d.wait_event(self._compute_done)
+            if inputs_free is not None:
+                h2d.wait_event(inputs_free)
             with torch.cuda.stream(h2d):
                 for b in range(self.nb):
                     copy_in(b)
@@ -269,7 +300,7 @@ class DccKvSyncLayer:
             if copy_in is not None:
                 main.wait_event(copied[b])
             if copy_out is not None:
-                main.wait_event(drained[b])  # the previous call's copy-out of this block
+                main.wait_event(drained[b])  # the last copy-out from this output buffer
             self._attention([self.attn_problems[b]])
             if copy_out is not None:
                 attended[b].record(main)
@@ -279,9 +310,8 @@ class DccKvSyncLayer:
                     drained[b].record(d2h)
         if self.nb == 1:
             main.wait_stream(side)
-        self._compute_done.record(main)
-        if copy_out is not None:
-            main.wait_stream(d2h)
+        if inputs_done is not None:
+            inputs_done.record(main)
 
     def _forward_host(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                       out: Optional[torch.Tensor]) -> torch.Tensor:
@@ -289,7 +319,9 @@ class DccKvSyncLayer:
         copy-in of block b (h2d) || pooling of b + builds s -> b (high-priority
         side stream) || attention of b (current stream) || copy-out of block
         b (d2h).  Block b's builds only need the keys / values of blocks
-        s < b, which arrived earlier, so the copies hide behind the compute."""
+        s < b, which arrived earlier, so the copies hide behind the compute.
+        Consecutive calls alternate between two device staging sets, so the
+        copy-in of one call overlaps the compute of the previous one."""
         exp_q = (self.nb, self.hq, self.L, self.d)
         exp_kv = (self.nb, self.hkv, self.L, self.d)
         for t, shp in ((q, exp_q), (k, exp_kv), (v, exp_kv)):
@@ -304,12 +336,30 @@ class DccKvSyncLayer:
             raise ValueError(f"out must be a contiguous CPU {self.dtype} tensor of shape {exp_q}")
         dev = self.device
         if self._staging is None:
-            self._staging = (torch.empty(exp_q, dtype=self.dtype, device=dev),
-                             torch.empty(exp_kv, dtype=self.dtype, device=dev),
-                             torch.empty(exp_kv, dtype=self.dtype, device=dev))
+            # two device staging sets (inputs and output), alternated by
+            # consecutive calls
+            self._staging = [(torch.empty(exp_q, dtype=self.dtype, device=dev),
+                              torch.empty(exp_kv, dtype=self.dtype, device=dev),
+                              torch.empty(exp_kv, dtype=self.dtype, device=dev),
+                              torch.empty(exp_q, dtype=self.dtype, device=dev)) for _ in range(2)]
+            # recorded once a call's compute no longer reads staging set i
+            self._staging_done = [None, None]
+            # per set and block: recorded after the copy-out of that block
+            self._drained = [[torch.cuda.Event() for _ in range(self.nb)] for _ in range(2)]
+            self._host_calls = 0
+            self._host_stream = torch.cuda.Stream(device=dev)
         self._ensure_streams()
-        dq, dk_, dv = self._staging
-        self._bind(dq, dk_, dv)
+        caller = torch.cuda.current_stream(dev)
+        if not self._last_call_host:
+            # device-path work on the caller's stream may still use the internal buffers
+            self._host_stream.wait_stream(caller)
+        self._last_call_host = True
+        i = self._host_calls % 2
+        self._host_calls += 1
+        dq, dk_, dv, dout = self._staging[i]
+        self._bind(dq, dk_, dv, dout)
+        free = self._staging_done[i]
+        self._staging_done[i] = torch.cuda.Event()
 
         def copy_in(b):
             dq[b].copy_(q[b], non_blocking=True)
@@ -317,9 +367,15 @@ class DccKvSyncLayer:
             dv[b].copy_(v[b], non_blocking=True)
 
         def copy_out(b):
-            out[b].copy_(self.out[b], non_blocking=True)
+            out[b].copy_(dout[b], non_blocking=True)
 
-        self._run_blocks(pool_all=False, copy_in=copy_in, copy_out=copy_out)
+        # the compute runs on an internal stream that does not wait for the
+        # copy-out, so the next call's compute can start under this call's
+        # last copies; the caller's stream waits for the output
+        with torch.cuda.stream(self._host_stream):
+            self._run_blocks(pool_all=False, copy_in=copy_in, copy_out=copy_out, inputs_free=free,
+                             inputs_done=self._staging_done[i], drained=self._drained[i])
+        caller.wait_stream(self._streams[2])
         return out
 
     def launches_per_forward(self) -> int:
