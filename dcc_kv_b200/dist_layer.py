@@ -153,20 +153,26 @@ class DistributedDccKvLayer:
         self.comm_stream = torch.cuda.Stream(device=dev, priority=hi)
         self._bound = None
         self._bindings = {}
+        self._host_stream = None
+        self._last_call_host = False
         self._ws, self._ws_bytes = None, 0
         self.timing_events = None
         self.timing_index = 0
 
-    def _bind(self, q, k, v):
-        """Point the kernel descriptors at q, k, v; descriptor sets are cached
-        per input buffers (the host-buffer path alternates between two device
-        staging sets) and the build workspace only grows."""
-        key = (q.data_ptr(), k.data_ptr(), v.data_ptr())
+    def _bind(self, q, k, v, o=None, lse=None):
+        """Point the kernel descriptors at q, k, v and the device output /
+        LSE buffers (default: the internal ``o_loc`` / ``lse_loc``);
+        descriptor sets are cached per buffers (the host-buffer path
+        alternates between two device staging sets) and the build workspace
+        only grows."""
+        o = self.o_loc if o is None else o
+        lse = self.lse_loc if lse is None else lse
+        key = (q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr())
         if self._bound == key:
             return
         bound = self._bindings.get(key)
         if bound is None:
-            bound = self._make_binding(q, k, v)
+            bound = self._make_binding(q, k, v, o, lse)
             if len(self._bindings) >= 4:
                 self._bindings.pop(next(iter(self._bindings)))
             self._bindings[key] = bound
@@ -177,7 +183,7 @@ class DistributedDccKvLayer:
             self._ws, self._ws_bytes = L.workspace(need, self.device), need
         self._bound = key
 
-    def _make_binding(self, q, k, v):
+    def _make_binding(self, q, k, v, o, lse):
         g = self.qgroup
         sets = [query_set(q[li, h * g], self.repr_local[li, h], self.repr_idx[li, h], n_seg=g,
                                seg_rows=self.window, seg_stride=q.stride(1), row_stride=q.stride(2))
@@ -196,7 +202,7 @@ class DistributedDccKvLayer:
         if build:
             arr = (L.dcc_build_problem * len(build))(*build)
             need = L.lib().dcc_build_compact_kv_workspace_bytes(arr, len(build), self.d, self.d, self.code)
-        local_problems = [attn_problem(q[li], self.o_loc[li], self.lse_loc[li], [kv_segment(k[li], v[li])],
+        local_problems = [attn_problem(q[li], o[li], lse[li], [kv_segment(k[li], v[li])],
                                        causal=True) for li in range(self.n_local)]
         recv_off = self.plan.recv_offsets(self.rank)
         # the compact blocks continue each local block's online softmax from
@@ -209,8 +215,7 @@ class DistributedDccKvLayer:
                 ko, vo, bo = self.plan.layout[(s, r)].views(self.bufs[buf], off, self.dtype)
                 segs.append(kv_segment(ko, vo, bo))
             if segs:
-                compact_problems.append(attn_problem(q[li], self.o_loc[li], None, segs,
-                                                     o_init=self.o_loc[li], lse_init=self.lse_loc[li]))
+                compact_problems.append(attn_problem(q[li], o[li], None, segs, o_init=o[li], lse_init=lse[li]))
         return sets, build, local_problems, compact_problems, need
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
@@ -230,6 +235,10 @@ class DistributedDccKvLayer:
                 raise ValueError(f"inputs must be contiguous {self.dtype}, all on {self.device} or all on the host")
         if host:
             return self._forward_host(q, k, v, out)
+        if self._host_stream is not None and self._last_call_host:
+            # the internal buffers were last used by the host-buffer path's stream
+            torch.cuda.current_stream(self.device).wait_stream(self._host_stream)
+        self._last_call_host = False
         self._bind(q, k, v)
         self._run()
         return self.o_loc
@@ -297,23 +306,35 @@ class DistributedDccKvLayer:
             raise ValueError(f"out must be a contiguous CPU {self.dtype} tensor of shape {exp_q}")
         dev = self.device
         if getattr(self, "_staging", None) is None:
-            # two device staging sets, alternated by consecutive calls, so the
-            # copy-in of one call overlaps the compute of the previous one
+            # two device staging sets (inputs, output, LSE), alternated by
+            # consecutive calls, so the copy-in of one call overlaps the
+            # compute of the previous one
             self._staging = [(torch.empty_like(q, device=dev), torch.empty_like(k, device=dev),
-                              torch.empty_like(v, device=dev)) for _ in range(2)]
+                              torch.empty_like(v, device=dev), torch.empty_like(self.o_loc),
+                              torch.empty_like(self.lse_loc)) for _ in range(2)]
             self._staging_done = [None, None]
             self._host_calls = 0
+            self._host_stream = torch.cuda.Stream(device=dev)
             self._h2d = torch.cuda.Stream(device=dev)
             self._d2h = torch.cuda.Stream(device=dev)
             self._ev_win, self._ev_kv = torch.cuda.Event(), torch.cuda.Event()
             self._ev_q = [torch.cuda.Event() for _ in range(self.n_local)]
             self._ev_merged = [torch.cuda.Event() for _ in range(self.n_local)]
-            self._ev_drained = [torch.cuda.Event() for _ in range(self.n_local)]
+            # per staging set and local block: recorded after its copy-out
+            self._ev_drained = [[torch.cuda.Event() for _ in range(self.n_local)] for _ in range(2)]
+        caller = torch.cuda.current_stream(dev)
+        if not self._last_call_host:
+            # device-path work on the caller's stream may still use the internal buffers
+            self._host_stream.wait_stream(caller)
+        self._last_call_host = True
         i = self._host_calls % 2
         self._host_calls += 1
-        dq, dk_, dv = self._staging[i]
-        self._bind(dq, dk_, dv)
-        main = torch.cuda.current_stream(dev)
+        dq, dk_, dv, do, dlse = self._staging[i]
+        self._bind(dq, dk_, dv, do, dlse)
+        # the compute runs on an internal stream that does not wait for the
+        # copy-out, so the next call's compute can start under this call's
+        # last copies; the caller's stream waits for the output
+        main = self._host_stream
         h2d, d2h = self._h2d, self._d2h
         W = self.window
         # the kernels of the call before the previous one must be done with
@@ -324,7 +345,7 @@ class DistributedDccKvLayer:
             h2d.wait_event(self._staging_done[i])
         self._staging_done[i] = torch.cuda.Event()
         for li in range(self.n_local):
-            main.wait_event(self._ev_drained[li])
+            main.wait_event(self._ev_drained[i][li])
         with torch.cuda.stream(h2d):
             for li in range(self.n_local):
                 for h in range(self.hq):
@@ -338,14 +359,15 @@ class DistributedDccKvLayer:
                     for h in range(self.hq):
                         dq[li, h, W:].copy_(q[li, h, W:], non_blocking=True)
                 self._ev_q[li].record(h2d)
-        self._run(self._ev_win, self._ev_kv, self._ev_q, self._ev_merged)
+        with torch.cuda.stream(main):
+            self._run(self._ev_win, self._ev_kv, self._ev_q, self._ev_merged)
         self._staging_done[i].record(main)
         with torch.cuda.stream(d2h):
             for li in range(self.n_local):
                 d2h.wait_event(self._ev_merged[li])
-                out[li].copy_(self.o_loc[li], non_blocking=True)
-                self._ev_drained[li].record(d2h)
-        main.wait_stream(d2h)
+                out[li].copy_(do[li], non_blocking=True)
+                self._ev_drained[i][li].record(d2h)
+        caller.wait_stream(d2h)
         return out
 
     def launches_per_forward(self) -> int:

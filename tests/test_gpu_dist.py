@@ -2,7 +2,8 @@
 single-GPU layer on the same inputs: every rank's blocks agree within the
 bf16 bar (2e-2); the two differ only in how the compact blocks are split
 into KV tiles.  The host-buffer call must reproduce the device call bit for
-bit.  Skipped on a box with fewer than 2 GPUs."""
+bit.  The single-rank case runs the same code on one GPU; the others are
+skipped on a box with fewer GPUs."""
 from __future__ import annotations
 
 import multiprocessing as pymp
@@ -44,23 +45,30 @@ def _worker(rank, world, port, errq):
         for li, b in enumerate(mine):
             err = ((out[li].float() - ref[b].float()).abs().max() / ref[b].float().abs().max()).item()
             assert err < 2e-2, f"block {b}: {err}"
-        # host buffers: copies pipelined with the compute, same kernels, same result
-        want = out.cpu()
-        hq, hk, hv = (t[mine].contiguous().pin_memory() for t in (q, k, v))
-        host_out = torch.empty(want.shape, dtype=want.dtype).pin_memory()
-        for _ in range(2):
-            layer(hq, hk, hv, out=host_out)
+        # host buffers: copies pipelined with the compute, same kernels, same
+        # result; three calls alternating two inputs (consecutive calls use
+        # alternate device staging sets and overlap one another)
+        want = [out.cpu()]
+        q2, k2, v2 = layer_inputs(NB, L, HQ, HKV, D, device="cpu", first_seed=29)
+        want.append(layer(q2[mine].contiguous().to(dev), k2[mine].contiguous().to(dev),
+                          v2[mine].contiguous().to(dev)).cpu())
+        hosts = [tuple(t[mine].contiguous().pin_memory() for t in x) for x in ((q, k, v), (q2, k2, v2))]
+        host_outs = [torch.empty(want[0].shape, dtype=want[0].dtype).pin_memory() for _ in range(3)]
+        for c in range(3):
+            layer(*hosts[c % 2], out=host_outs[c])
         torch.cuda.synchronize()
-        assert torch.equal(host_out, want)
+        for c in range(3):
+            assert torch.equal(host_outs[c], want[c % 2]), c
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
         errq.put(traceback.format_exc())
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_distributed_layer_matches_single_gpu():
-    world = 2
+@pytest.mark.parametrize("world", [1, 2])
+def test_distributed_layer_matches_single_gpu(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
     ctx = pymp.get_context("spawn")
     errq = ctx.Queue()
     port = random.randint(20000, 40000)
