@@ -433,6 +433,63 @@ def profile_attention(args):
     print("profiled attention launch done", flush=True)
 
 
+def exchange_study(args):
+    """Communication-computation overlap of the compact-KV exchange (the
+    reference's sync-vs-async question, tests/gpu/test_async_overlap.py):
+    per-layer time with the pooling, builds and all-to-allv on the main stream
+    before any attention (sync), on the side stream under the local attention
+    (async, the default), and for ``--layers`` layers in a row with the
+    exchange double buffered across layers (stack).  Not the bench line."""
+    from dcc_kv_b200.dist_layer import DistributedDccKvLayer, DistributedDccKvStack
+    from dcc_kv_b200.workloads import gqa_block
+    ws, rank, dev = _setup_dist()
+    if ws < 2:
+        print(json.dumps({"study": "exchange overlap", "unavailable": "needs 2+ GPUs under torchrun"}))
+        return
+    blocks = [b for b in range(N_BLOCKS) if b % ws == rank]
+    inputs = []
+    for layer_i in range(args.layers):
+        parts = [gqa_block(HQ, HKV, BLOCK_LEN, D, 1000 * (layer_i + 1) + b, device="cuda") for b in blocks]
+        inputs.append(tuple(torch.stack([p_[i] for p_ in parts]) for i in range(3)))
+    kw = dict(device=dev)
+    layer = DistributedDccKvLayer(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, **kw)
+    stack = DistributedDccKvStack(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, **kw)
+    stream = torch.cuda.current_stream(dev)
+
+    def timed(fn):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        _barrier(ws)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(args.steps):
+            fn()
+        e1.record(stream)
+        _barrier(ws)
+        return _max_over_ranks(e0.elapsed_time(e1) / args.steps / args.layers, ws)
+
+    def layer_by_layer():
+        for x in inputs:
+            layer(*x)
+
+    layer.overlap_exchange = False
+    t_sync = timed(layer_by_layer)
+    layer.overlap_exchange = True
+    t_async = timed(layer_by_layer)
+    t_stack = timed(lambda: stack(inputs))
+    plan = layer.plan
+    if rank == 0:
+        print(json.dumps({
+            "study": "exchange overlap", "n_gpus": ws, "layers": args.layers, "steps": args.steps,
+            "config": dict(WORKLOAD, parallelism=f"context parallel over {ws} GPUs"),
+            "exchange_bytes_per_rank_per_layer": max(sum(plan.send_splits(r)) for r in range(ws)),
+            "ms_per_layer": {"sync": t_sync, "async": t_async, "stack": t_stack},
+            "speedup_async_vs_sync": t_sync / t_async, "speedup_stack_vs_sync": t_sync / t_stack,
+        }), flush=True)
+    del stack, layer
+    _teardown(ws)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -445,8 +502,14 @@ def main():
                          "overlapped with per-block attention")
     ap.add_argument("--profile-attention", action="store_true",
                     help="run two attention launches of one block (small case for ncu) and exit")
+    ap.add_argument("--exchange-study", action="store_true",
+                    help="under torchrun, N >= 2: time the compact exchange synchronous, overlapped, and "
+                         "double buffered across --layers layers, and exit")
+    ap.add_argument("--layers", type=int, default=4, help="layers in a row for --exchange-study")
     args = ap.parse_args()
-    if args.profile_attention:
+    if args.exchange_study:
+        exchange_study(args)
+    elif args.profile_attention:
         profile_attention(args)
     elif args.impl == "reference":
         run_reference(args)

@@ -151,6 +151,9 @@ class DistributedDccKvLayer:
         # attention that fills the GPU meanwhile on the main stream
         lo, hi = torch.cuda.Stream.priority_range()
         self.comm_stream = torch.cuda.Stream(device=dev, priority=hi)
+        # False: pooling, builds and exchange on the main stream before any
+        # attention (no communication-computation overlap; same outputs)
+        self.overlap_exchange = True
         self._bound = None
         self._bindings = {}
         self._host_stream = None
@@ -173,7 +176,7 @@ class DistributedDccKvLayer:
         bound = self._bindings.get(key)
         if bound is None:
             bound = self._make_binding(q, k, v, o, lse)
-            if len(self._bindings) >= 4:
+            if len(self._bindings) >= 8:
                 self._bindings.pop(next(iter(self._bindings)))
             self._bindings[key] = bound
         self.sets, self.build, self.local_problems, self.compact_problems, need = bound
@@ -257,15 +260,27 @@ class DistributedDccKvLayer:
         if ev is not None:
             ev[1].record(main)
 
-    def _run(self, windows_ready=None, kv_ready=None, q_ready=None, merged=None) -> None:
+    def _run(self, windows_ready=None, kv_ready=None, q_ready=None, merged=None, side_waits=None,
+             done=None) -> None:
         """One forward on bound buffers.  The optional per-phase events gate
         the work on host-to-device copies (pooling on the query windows,
         builds on K / V, local attention of block li on its queries) and
-        ``merged[li]`` is recorded once block li's output is final."""
+        ``merged[li]`` is recorded once block li's output is final.  The side
+        stream waits for the main stream (inputs written, the previous
+        forward done with the exchange buffers) unless ``side_waits`` names
+        the events to wait for instead; ``done`` is recorded after the
+        compact attention, the last reader of the exchange buffers.  With
+        ``overlap_exchange`` off, the pooling, builds and exchange run on the
+        main stream before any attention (the synchronous baseline)."""
         dev = self.device
         main = torch.cuda.current_stream(dev)
-        side = self.comm_stream
-        side.wait_stream(main)  # inputs written, previous step's buffers released
+        side = self.comm_stream if self.overlap_exchange else main
+        if side is not main:
+            if side_waits is None:
+                side.wait_stream(main)  # inputs written, previous step's buffers released
+            else:
+                for e in side_waits:
+                    side.wait_event(e)
         with torch.cuda.stream(side):
             if windows_ready is not None:
                 side.wait_event(windows_ready)
@@ -287,6 +302,8 @@ class DistributedDccKvLayer:
                 self._attention([self.local_problems[li]])
         main.wait_stream(side)
         run_attention(self.compact_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code, dev)
+        if done is not None:
+            done.record(main)
         if merged is not None:
             for li in range(self.n_local):
                 merged[li].record(main)
@@ -375,3 +392,56 @@ class DistributedDccKvLayer:
         pool = 0 if sets == 0 else 2 * -(-sets // 64)
         return (pool + build_launch_count(len(self.build), self.code, self.d) + -(-len(self.local_problems) // 8)
                 + -(-len(self.compact_problems) // 8))
+
+
+class DistributedDccKvStack:
+    """Several DCC-KV sync layers in a row (one process per GPU, each layer
+    with its own local q / k / v, as ``DistributedDccKvLayer``), with the
+    compact-KV exchange double buffered across layers: two layer slots, each
+    with its own compact, receive, representative-query and workspace
+    buffers, take the layers in turn, and a slot's pooling, builds and
+    all-to-allv (its high-priority side stream) wait only for the inputs and
+    for the compact attention of the layer two back.  So layer l + 1's
+    exchange runs while layer l's attention runs (the reference's
+    asynchronous-exchange pipeline, tests/gpu/test_async_overlap.py:43-98).
+    Every layer writes its own output buffer; outputs equal those of the
+    layers called one at a time, bit for bit."""
+
+    def __init__(self, *args, **kwargs):
+        self.slots = [DistributedDccKvLayer(*args, **kwargs) for _ in range(2)]
+        self._outs: List[torch.Tensor] = []
+        self._done = [None, None]
+
+    def forward(self, inputs) -> List[torch.Tensor]:
+        """inputs: a sequence of (q, k, v) device tensors per layer, shaped
+        as for ``DistributedDccKvLayer``.  Returns one output per layer
+        (internal buffers, reused by the next call); complete once the
+        current stream is synchronized."""
+        first = self.slots[0]
+        dev = first.device
+        main = torch.cuda.current_stream(dev)
+        exp_q = (first.n_local, first.hq, first.L, first.d)
+        exp_kv = (first.n_local, first.hkv, first.L, first.d)
+        while len(self._outs) < len(inputs):
+            self._outs.append(torch.empty(exp_q, dtype=first.dtype, device=dev))
+        ready = torch.cuda.Event()
+        ready.record(main)  # every layer's inputs are written
+        for li, (q, k, v) in enumerate(inputs):
+            if tuple(q.shape) != exp_q or tuple(k.shape) != exp_kv or tuple(v.shape) != exp_kv:
+                raise ValueError(f"layer {li}: expected local q {exp_q}, k/v {exp_kv}")
+            for t in (q, k, v):
+                if t.dtype != first.dtype or not t.is_contiguous() or t.device != dev:
+                    raise ValueError(f"layer {li}: inputs must be contiguous {first.dtype} on {dev}")
+            slot = self.slots[li % 2]
+            if slot._host_stream is not None and slot._last_call_host:
+                main.wait_stream(slot._host_stream)
+            slot._last_call_host = False
+            slot._bind(q, k, v, self._outs[li], slot.lse_loc)
+            prev = self._done[li % 2]
+            waits = [ready] + ([prev] if prev is not None else [])
+            done = torch.cuda.Event()
+            slot._run(side_waits=waits, done=done)
+            self._done[li % 2] = done
+        return self._outs[:len(inputs)]
+
+    __call__ = forward

@@ -87,6 +87,64 @@ def test_distributed_layer_matches_single_gpu(world):
     assert all(p.exitcode == 0 for p in procs)
 
 
+def _stack_worker(rank, world, port, errq):
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        from dcc_kv_b200.dist_layer import DistributedDccKvLayer, DistributedDccKvStack
+        from dcc_kv_b200.workloads import layer_inputs
+        mine = [b for b in range(NB) if b % world == rank]
+        inputs = []
+        for seed in (11, 29, 47):
+            q, k, v = layer_inputs(NB, L, HQ, HKV, D, device="cpu", first_seed=seed)
+            inputs.append(tuple(t[mine].contiguous().to(dev) for t in (q, k, v)))
+        layer = DistributedDccKvLayer(NB, L, HQ, HKV, D, BUDGETS, window=128, device=dev)
+        want = [layer(*x).clone() for x in inputs]
+        # no communication-computation overlap: same kernels, same outputs
+        layer.overlap_exchange = False
+        for x, w in zip(inputs, want):
+            assert torch.equal(layer(*x), w)
+        # exchange of layer l + 1 overlapped with the attention of layer l
+        stack = DistributedDccKvStack(NB, L, HQ, HKV, D, BUDGETS, window=128, device=dev)
+        for _ in range(2):  # second call reuses every buffer
+            outs = stack(inputs)
+            torch.cuda.synchronize()
+            for li, (o, w) in enumerate(zip(outs, want)):
+                assert torch.equal(o, w), f"layer {li}"
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put(traceback.format_exc())
+
+
+@pytest.mark.parametrize("world", [1, 2])
+def test_layer_stack_double_buffered_exchange_matches_layer_by_layer(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = pymp.get_context("spawn")
+    errq = ctx.Queue()
+    port = random.randint(20000, 40000)
+    procs = [ctx.Process(target=_stack_worker, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not errors, "\n".join(errors)
+    assert all(p.exitcode == 0 for p in procs)
+
+
 def _ring_worker(rank, world, port, errq):
     try:
         import datetime
