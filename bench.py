@@ -311,11 +311,13 @@ def run_gpu(args):
         parallelism = f"single GPU, 8 logical blocks, {args.schedule} schedule"
     else:
         from dcc_kv_b200.dist_layer import DistributedDccKvLayer
-        blocks = [b for b in range(N_BLOCKS) if b % ws == rank]
+        from dcc_kv_b200.dist_layer import local_blocks_of
+        blocks = local_blocks_of(N_BLOCKS, ws, rank)
         parts = [gqa_block(HQ, HKV, BLOCK_LEN, D, 1000 + b, device="cuda") for b in blocks]
         q, k, v = (torch.stack([p_[i] for p_ in parts]) for i in range(3))
         layer = DistributedDccKvLayer(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, device=dev)
-        parallelism = f"context parallel over {ws} GPUs (block b on rank b % {ws}), NCCL all-to-allv of compacts"
+        parallelism = (f"context parallel over {ws} GPUs (blocks dealt to ranks in snake order), "
+                       "NCCL all-to-allv of compacts")
     stream = torch.cuda.current_stream(dev)
     warmup = max(args.warmup, 3)
     for _ in range(warmup):
@@ -446,7 +448,8 @@ def exchange_study(args):
     if ws < 2:
         print(json.dumps({"study": "exchange overlap", "unavailable": "needs 2+ GPUs under torchrun"}))
         return
-    blocks = [b for b in range(N_BLOCKS) if b % ws == rank]
+    from dcc_kv_b200.dist_layer import local_blocks_of
+    blocks = local_blocks_of(N_BLOCKS, ws, rank)
     inputs = []
     for layer_i in range(args.layers):
         parts = [gqa_block(HQ, HKV, BLOCK_LEN, D, 1000 * (layer_i + 1) + b, device="cuda") for b in blocks]

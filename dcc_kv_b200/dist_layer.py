@@ -1,8 +1,10 @@
 """The DCC-KV sync layer sharded by sequence block over one process per GPU.
 
-Logical block b lives on rank b % G (round-robin, so the causal load --
-more compact blocks for later blocks, more builds for earlier ones --
-balances across ranks).  One forward on every rank:
+Logical blocks are dealt to ranks in snake order (0, 1, .., G-1, G-1, ..,
+1, 0, 0, 1, ..): block r attends to r compact blocks and block s builds
+n_blocks - 1 - s edges, so pairing block b with its mirror n_blocks - 1 - b
+on one rank balances both (for 8 blocks on 4 ranks every rank gets 7 compact
+blocks; round-robin would give 4 to 10).  One forward on every rank:
 
   0. pooling: representative queries of the local destination blocks
      (FP64 FPS), then ``all_gather`` of the [n_local, H_kv, M, d] tensors
@@ -40,6 +42,18 @@ from .representative_query import query_set, select_query_sets
 from .var_len_msg import EdgeLayout
 
 
+def block_owner(b: int, world: int) -> int:
+    """Rank of logical block b: snake order over the ranks."""
+    m = b % (2 * world)
+    return m if m < world else 2 * world - 1 - m
+
+
+def local_blocks_of(n_blocks: int, world: int, rank: int) -> List[int]:
+    """The logical blocks of ``rank`` in ascending order -- the order of the
+    local block dimension of its inputs and outputs."""
+    return [b for b in range(n_blocks) if block_owner(b, world) == rank]
+
+
 class DistPlan:
     """Routing of every compact-KV edge (s -> r, s < r) for G ranks."""
 
@@ -59,13 +73,13 @@ class DistPlan:
         self.bytes_ij = {ij: sum(self.layout[e].nbytes for e in es) for ij, es in self.edges_ij.items()}
 
     def owner(self, b: int) -> int:
-        return b % self.world
+        return block_owner(b, self.world)
 
     def local_index(self, b: int) -> int:
-        return b // self.world
+        return self.local_blocks(self.owner(b)).index(b)
 
     def local_blocks(self, rank: int) -> List[int]:
-        return [b for b in range(self.nb) if self.owner(b) == rank]
+        return local_blocks_of(self.nb, self.world, rank)
 
     def send_splits(self, rank: int) -> List[int]:
         return [0 if j == rank else self.bytes_ij[(rank, j)] for j in range(self.world)]
@@ -106,7 +120,7 @@ class DistPlan:
 class DistributedDccKvLayer:
     """One process per GPU; block-major local inputs
     q [n_local, H_q, L, d], k / v [n_local, H_kv, L, d] for the blocks
-    rank, rank + G, rank + 2G, ... of the context."""
+    ``local_blocks_of(n_blocks, G, rank)`` of the context, ascending."""
 
     def __init__(self, n_blocks: int, block_len: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
                  budgets: Budgets, window: int, num_representative_queries: int = 64, projection_dim: int = 32,

@@ -61,8 +61,23 @@ def test_plan_routes_every_edge_once(world):
     for i in range(world):
         for j in range(world):
             assert plan.send_splits(i)[j] == plan.recv_splits(j)[i]
-    # every block sits on exactly one rank, round-robin
+    # every block sits on exactly one rank, and the local index is its
+    # position among the rank's blocks
     assert sorted(b for r in range(world) for b in plan.local_blocks(r)) == list(range(8))
+    for b in range(8):
+        assert plan.local_blocks(plan.owner(b))[plan.local_index(b)] == b
+
+
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_snake_mapping_balances_compact_and_build_work(world):
+    """Block r attends to r compact blocks and block s builds 7 - s edges:
+    with 8 blocks on 1, 2 or 4 ranks the snake order gives every rank the
+    same amount of both (on 8 ranks each rank holds one block)."""
+    from dcc_kv_b200.dist_layer import local_blocks_of
+    parts = [local_blocks_of(8, world, r) for r in range(world)]
+    assert sorted(b for p in parts for b in p) == list(range(8))
+    assert len({sum(p) for p in parts}) == 1
+    assert len({sum(7 - b for b in p) for p in parts}) == 1
 
 
 def test_plan_rejects_uneven_split():

@@ -34,7 +34,8 @@ def _worker(rank, world, port, errq):
         from dcc_kv_b200.dist_layer import DistributedDccKvLayer
         from dcc_kv_b200.workloads import layer_inputs
         q, k, v = layer_inputs(NB, L, HQ, HKV, D, device="cpu", first_seed=11)
-        mine = [b for b in range(NB) if b % world == rank]
+        from dcc_kv_b200.dist_layer import local_blocks_of
+        mine = local_blocks_of(NB, world, rank)
         layer = DistributedDccKvLayer(NB, L, HQ, HKV, D, BUDGETS, window=128, device=dev)
         out = None
         for _ in range(2):  # second call reuses every buffer
@@ -99,7 +100,8 @@ def _stack_worker(rank, world, port, errq):
                                 device_id=dev)
         from dcc_kv_b200.dist_layer import DistributedDccKvLayer, DistributedDccKvStack
         from dcc_kv_b200.workloads import layer_inputs
-        mine = [b for b in range(NB) if b % world == rank]
+        from dcc_kv_b200.dist_layer import local_blocks_of
+        mine = local_blocks_of(NB, world, rank)
         inputs = []
         for seed in (11, 29, 47):
             q, k, v = layer_inputs(NB, L, HQ, HKV, D, device="cpu", first_seed=seed)
