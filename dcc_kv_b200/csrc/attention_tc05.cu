@@ -82,30 +82,25 @@ struct Smem {
   unsigned char k[2][kTileBytes];    // stages
   unsigned char v[2][kTileBytes];
   __align__(16) float bias[2][kKeys];
-  int64_t kend[kTcMaxSeg];  // segment ends clipped by the causal limit
   uint64_t bar_q, bar_k[2], bar_v[2], bar_bias[2], bar_empty[2], bar_s[2], bar_p[2], bar_o[2];
   uint32_t tmem;
 };
 
-// Walks this CTA's KV tiles in order (segments in order, 128 keys per tile,
-// empty segments skipped); the clipped segment ends live in shared memory.
-struct TileCursor {
+struct Tile {
   int seg;
   int64_t t0;
-  __device__ __forceinline__ void start(const int64_t* kend, int n_seg) {
-    seg = 0;
-    t0 = 0;
-    while (seg < n_seg && kend[seg] <= 0) ++seg;
-  }
-  __device__ __forceinline__ void next(const int64_t* kend, int n_seg) {
-    t0 += kKeys;
-    if (t0 >= kend[seg]) {
-      t0 = 0;
-      ++seg;
-      while (seg < n_seg && kend[seg] <= 0) ++seg;
-    }
-  }
+  int64_t kend;
 };
+
+// The j-th KV tile of this CTA (segments in order, 128 keys per tile).
+__device__ __forceinline__ Tile tile_at(const Tc05Problem& p, const int64_t* kend, int j) {
+  for (int s = 0; s < p.n_seg; ++s) {
+    const int nt = (int)((kend[s] + kKeys - 1) / kKeys);
+    if (j < nt) return Tile{s, (int64_t)j * kKeys, kend[s]};
+    j -= nt;
+  }
+  return Tile{0, 0, 0};
+}
 
 __device__ __forceinline__ uint64_t kdesc(const unsigned char* tile, int kk) {
   // K-major operand: 16-column step kk inside column block kk / 4
@@ -139,7 +134,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 using namespace fa;
 
 // ---- TMA producer (warp 8) --------------------------------------------------------
-__device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, int n_tiles,
+__device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, const int64_t* kend, int n_tiles,
                                               int64_t q0, int hA, int hB, int hk, int lane) {
   bool ok = true;
   if (lane == 0) {
@@ -151,14 +146,13 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, in
     tma_load_3d(sm.q[1] + 16384, &p.q, &sm.bar_q, 64, (int)q0, hB);
   }
   int issued = 0;
-  TileCursor t;
-  t.start(sm.kend, p.n_seg);
-  for (int j = 0; j < n_tiles; ++j, t.next(sm.kend, p.n_seg)) {
+  for (int j = 0; j < n_tiles; ++j) {
     const int st = j & 1;
     if (j >= 2 && !warp_wait(&sm.bar_empty[st], ((j >> 1) - 1) & 1)) {
       ok = false;
       break;
     }
+    const Tile t = tile_at(p, kend, j);
     const Tc05Seg& sg = p.seg[t.seg];
     if (lane == 0) {
       mbar_expect_tx(&sm.bar_k[st], kTileBytes);
@@ -173,7 +167,7 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, in
     for (int i = 0; i < 4; ++i) {
       const int c = lane * 4 + i;
       const int64_t key = t.t0 + c;
-      sm.bias[st][c] = (bg && key < sm.kend[t.seg]) ? __ldg(bg + key) * 1.4426950408889634f : 0.f;  // log2 units
+      sm.bias[st][c] = (bg && key < t.kend) ? __ldg(bg + key) * 1.4426950408889634f : 0.f;  // log2 units
     }
     mbar_arrive(&sm.bar_bias[st]);
     issued = j + 1;
@@ -193,7 +187,8 @@ __device__ __forceinline__ void producer_role(const Tc05Problem& p, Smem& sm, in
 // Issue order per tile j:  PV_A(j), S_A(j+1), PV_B(j), S_B(j+1)  (S_A(0), S_B(0) first),
 // so head A's next scores are ready while head B's softmax still runs.  S(j+1)
 // overwrites P(j) in TMEM only after PV(j), issued earlier from this thread.
-__device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int lane, bool acc0) {
+template <bool kInit>
+__device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int lane) {
   const uint32_t id_s = idesc_bf16_f32(128, 128, 0, 0);
   const uint32_t id_pv = idesc_bf16_f32(128, 128, 0, 1);
   bool ok = warp_wait(&sm.bar_q, 0);
@@ -212,7 +207,7 @@ __device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int
       const uint32_t o_col = h ? kColOB : kColOA, p_col = h ? kColSB : kColSA;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk)
-        umma_ts(tm + o_col, tm + p_col + kk * 8, vdesc(sm.v[st], kk), id_pv, (acc0 || j > 0 || kk > 0) ? 1u : 0u);
+        umma_ts(tm + o_col, tm + p_col + kk * 8, vdesc(sm.v[st], kk), id_pv, (kInit || j > 0 || kk > 0) ? 1u : 0u);
       umma_commit(&sm.bar_o[h]);
     }
     __syncwarp();
@@ -259,22 +254,22 @@ __device__ __forceinline__ void mma_role(Smem& sm, int n_tiles, uint32_t tm, int
 }
 
 // ---- softmax + epilogue (warps 0-3: head A, 4-7: head B) ------------------------
+template <bool kInit>
 __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Problem& p, Smem& sm,
-                                             int n_tiles, int64_t q0, int hA, int hB,
+                                             const int64_t* kend, int n_tiles, int64_t q0, int hA, int hB,
                                              uint32_t tm, int warp, int lane) {
   const int role = warp >> 2;
   const int row = (warp & 3) * 32 + lane;
   const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
   const uint32_t s_col = role ? kColSB : kColSA, o_col = role ? kColOB : kColOA;
   const int64_t q_row = q0 + row;
-  const int h = role ? hB : hA;
   float m_use = -INFINITY, l = 0.f;
   bool ok = true;
   // Optional initial state (m = lse_init, l = 1, O = o_init): O goes to TMEM
   // before the first P hand-off (whose tcgen05.wait::st covers these stores);
   // rows past Lq or without keys so far start empty.
-  const bool init = p.o_init != nullptr;
-  if (init) {
+  if (kInit) {
+    const int h = role ? hB : hA;
     const bool real = q_row < p.Lq;
     const float lse0 = real ? p.lse_init[h * p.lse_init_head_stride + q_row] : -INFINITY;
     const bool have = lse0 > -INFINITY;
@@ -301,11 +296,10 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     }
     tmem_wait_st();
   }
-  TileCursor t;
-  t.start(sm.kend, p.n_seg);
-  for (int j = 0; j < n_tiles; ++j, t.next(sm.kend, p.n_seg)) {
+  for (int j = 0; j < n_tiles; ++j) {
     const int st = j & 1;
-    const int64_t t_end = sm.kend[t.seg];
+    const Tile t = tile_at(p, kend, j);
+    const int64_t t_end = t.kend;
     const bool causal = p.causal && t.seg == 0;
     if (!warp_wait(&sm.bar_s[role], j & 1)) {
       ok = false;
@@ -363,7 +357,7 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     const bool need = mt > m_use + 8.f;
     if (__any_sync(0xffffffffu, need)) {
       const float corr = !need ? 1.f : (m_use == -INFINITY ? 0.f : exp2f(m_use - mt));
-      if (j > 0 || init) {
+      if (j > 0 || kInit) {
         if (j > 0 && !warp_wait(&sm.bar_o[role], (j - 1) & 1)) {
           ok = false;
           break;
@@ -409,6 +403,7 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     mbar_arrive(&sm.bar_p[role]);
   }
   if (!ok) atomicOr(&g_attn_error, 4u);
+  const int h = role ? hB : hA;
   if (ok && n_tiles > 0 && !warp_wait(&sm.bar_o[role], (n_tiles - 1) & 1)) {
     ok = false;
     atomicOr(&g_attn_error, 8u);
@@ -421,7 +416,7 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
 #pragma unroll 1
   for (int c = 0; c < 4; ++c) {
     uint32_t r[32];
-    if (n_tiles > 0 || init) {
+    if (n_tiles > 0 || kInit) {
       tmem_ld32(tm + lane_off + o_col + 32 * c, r);
       tmem_wait_ld();
     } else {
@@ -444,6 +439,9 @@ __device__ __forceinline__ void softmax_role(const Tc05Batch& b, const Tc05Probl
     p.lse[h * p.lse_head_stride + q_row] = (ok && l > 0.f) ? (m_use + log2f(l)) * 0.6931471805599453f : -INFINITY;
 }
 
+// kInit: every problem of the batch carries an initial state (a separate
+// instantiation, so the plain launch carries no code for it)
+template <bool kInit>
 __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_constant__ Tc05Batch b) {
   extern __shared__ unsigned char smem_raw[];
   Smem& sm = *reinterpret_cast<Smem*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
@@ -455,6 +453,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_con
   const int hA = 2 * blockIdx.y, hB = hA + 1, hk = hA / b.group;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
+  int64_t kend[kTcMaxSeg];
   int n_tiles = 0;
   for (int s = 0; s < kTcMaxSeg; ++s) {
     int64_t e = s < p.n_seg ? p.seg[s].len : 0;
@@ -462,9 +461,8 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_con
       const int64_t last = (q0 + kRows - 1 < p.Lq - 1 ? q0 + kRows - 1 : p.Lq - 1) + p.causal_offset + 1;
       e = e < last ? e : last;
     }
-    e = e > 0 ? e : 0;
-    if (threadIdx.x == 0) sm.kend[s] = e;
-    n_tiles += (int)((e + kKeys - 1) / kKeys);
+    kend[s] = e > 0 ? e : 0;
+    n_tiles += (int)((kend[s] + kKeys - 1) / kKeys);
   }
 
   if (threadIdx.x == 0) {
@@ -490,11 +488,11 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_con
   const uint32_t tm = sm.tmem;
   if (warp >= 8) {
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kRegsOther));
-    if (warp == 8) producer_role(p, sm, n_tiles, q0, hA, hB, hk, lane);
-    else if (warp == 9) mma_role(sm, n_tiles, tm, lane, p.o_init != nullptr);
+    if (warp == 8) producer_role(p, sm, kend, n_tiles, q0, hA, hB, hk, lane);
+    else if (warp == 9) mma_role<kInit>(sm, n_tiles, tm, lane);
   } else {
     asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kRegsSoftmax));
-    softmax_role(b, p, sm, n_tiles, q0, hA, hB, tm, warp, lane);
+    softmax_role<kInit>(b, p, sm, kend, n_tiles, q0, hA, hB, tm, warp, lane);
   }
   tc_fence_before();
   __syncthreads();
@@ -504,45 +502,64 @@ __global__ void __launch_bounds__(kThreads, 1) attn_tc05_kernel(const __grid_con
 static size_t tc05_smem_bytes() { return sizeof(Smem) + 1024; }
 
 // Host: build the batch (tensor maps per problem and segment) and launch.
-int launch_attn_tc05(const dcc_attn_problem* probs, int n, const AttnParams& prm, cudaStream_t st) {
-  DCC_CHECK(check_cuda(cudaFuncSetAttribute(attn_tc05_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+// Problems with and without an initial state go to separate launches of the
+// two kernel instantiations.
+template <bool kInit>
+static int tc05_prepare() {
+  DCC_CHECK(check_cuda(cudaFuncSetAttribute(attn_tc05_kernel<kInit>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                             (int)tc05_smem_bytes()),
                        "attn_tc05 smem"));
   // The setmaxnreg split assumes the kernel launches with kRegsLaunch registers
   // per thread; a smaller launch allocation would make setmaxnreg.inc wait forever.
   cudaFuncAttributes fa{};
-  DCC_CHECK(check_cuda(cudaFuncGetAttributes(&fa, attn_tc05_kernel), "attn_tc05 attributes"));
+  DCC_CHECK(check_cuda(cudaFuncGetAttributes(&fa, attn_tc05_kernel<kInit>), "attn_tc05 attributes"));
   if (fa.numRegs < kRegsLaunch)
     return fail(DCC_ERR_UNSUPPORTED, "attn_tc05: compiled with " + std::to_string(fa.numRegs) +
                                          " registers per thread, the register split needs " +
                                          std::to_string(kRegsLaunch));
+  return DCC_OK;
+}
+
+template <bool kInit>
+static int tc05_launch(const Tc05Batch& b, int64_t max_lq, const AttnParams& prm, cudaStream_t st) {
+  dim3 grid((unsigned)((max_lq + 127) / 128), prm.n_q_heads / 2, b.n);
+  attn_tc05_kernel<kInit><<<grid, kThreads, tc05_smem_bytes(), st>>>(b);
+  const cudaError_t le = cudaGetLastError();
+  if (le != cudaSuccess) {
+    cudaFuncAttributes fa{};
+    cudaFuncGetAttributes(&fa, attn_tc05_kernel<kInit>);
+    return fail(DCC_ERR_CUDA, std::string("attn_tc05 launch: ") + cudaGetErrorString(le) + " (" +
+                                  std::to_string(fa.numRegs) + " registers, max " +
+                                  std::to_string(fa.maxThreadsPerBlock) + " threads, " +
+                                  std::to_string(tc05_smem_bytes()) + " B dynamic shared memory)");
+  }
+  return DCC_OK;
+}
+
+int launch_attn_tc05(const dcc_attn_problem* probs, int n, const AttnParams& prm, cudaStream_t st) {
+  bool any_init = false, any_plain = false;
+  for (int i = 0; i < n; ++i) (probs[i].o_init ? any_init : any_plain) = true;
+  if (any_plain) DCC_CHECK(tc05_prepare<false>());
+  if (any_init) DCC_CHECK(tc05_prepare<true>());
   Tc05Batch* bp = new Tc05Batch();
   std::unique_ptr<Tc05Batch> own(bp);
   Tc05Batch& b = *bp;
   b.group = prm.group;
   b.scale_log2 = (float)(prm.scale * 1.4426950408889634);
   int64_t max_lq = 0;
+  bool batch_init = false;
   auto flush = [&]() -> int {
     if (b.n == 0) return DCC_OK;
-    if (max_lq > 0) {
-      dim3 grid((unsigned)((max_lq + 127) / 128), prm.n_q_heads / 2, b.n);
-      attn_tc05_kernel<<<grid, kThreads, tc05_smem_bytes(), st>>>(b);
-      const cudaError_t le = cudaGetLastError();
-      if (le != cudaSuccess) {
-        cudaFuncAttributes fa{};
-        cudaFuncGetAttributes(&fa, attn_tc05_kernel);
-        return fail(DCC_ERR_CUDA, std::string("attn_tc05 launch: ") + cudaGetErrorString(le) + " (" +
-                                      std::to_string(fa.numRegs) + " registers, max " +
-                                      std::to_string(fa.maxThreadsPerBlock) + " threads, " +
-                                      std::to_string(tc05_smem_bytes()) + " B dynamic shared memory)");
-      }
-    }
+    if (max_lq > 0) DCC_CHECK(batch_init ? tc05_launch<true>(b, max_lq, prm, st) : tc05_launch<false>(b, max_lq, prm, st));
     b.n = 0;
     max_lq = 0;
     return DCC_OK;
   };
   for (int i = 0; i < n; ++i) {
     const dcc_attn_problem& q = probs[i];
+    const bool init = q.o_init != nullptr;
+    if (b.n > 0 && init != batch_init) DCC_CHECK(flush());
+    batch_init = init;
     Tc05Problem& t = b.p[b.n];
     t = Tc05Problem{};
     if (q.Lq > 0)  // an empty problem launches no CTA and needs no map
