@@ -29,7 +29,7 @@ identical on every rank and testable without a GPU.
 from __future__ import annotations
 
 import math
-from typing import Dict, List, Tuple
+from typing import Dict, List, Optional, Tuple
 
 import torch
 import torch.distributed as dist
@@ -38,6 +38,7 @@ from . import _lib as L
 from .attention import attn_problem, kv_segment, run_attention
 from .compact_kv import build_launch_count, build_problem, run_build_problems
 from .layer import Budgets, budget_table
+from .online_softmax import merge_lse
 from .representative_query import query_set, select_query_sets
 from .var_len_msg import EdgeLayout
 
@@ -54,11 +55,28 @@ def local_blocks_of(n_blocks: int, world: int, rank: int) -> List[int]:
     return [b for b in range(n_blocks) if block_owner(b, world) == rank]
 
 
+def default_help(n_blocks: int, world: int) -> Dict[int, int]:
+    """With one block per rank the compact attention is unbalanced (block r
+    attends to r compact blocks): block r > its mirror p = n_blocks - 1 - r
+    hands its first (r - p) // 2 sources to p's rank, which computes that
+    part of r's compact attention.  Returns {r: number of helped sources}."""
+    if world != n_blocks:
+        return {}
+    help_ = {}
+    for r in range(n_blocks):
+        p = n_blocks - 1 - r
+        if r > p and (r - p) // 2 > 0:
+            help_[r] = (r - p) // 2
+    return help_
+
+
 class DistPlan:
-    """Routing of every compact-KV edge (s -> r, s < r) for G ranks."""
+    """Routing of every compact-KV edge (s -> r, s < r) for G ranks.  An edge
+    goes to the rank that consumes it: the owner of r, or, for the first
+    ``help[r]`` sources of a helped block r, the owner of r's mirror block."""
 
     def __init__(self, n_blocks: int, world: int, block_len: int, n_kv_heads: int, head_dim: int,
-                 budgets: Budgets, elem_bytes: int = 2):
+                 budgets: Budgets, elem_bytes: int = 2, help_sources: Optional[Dict[int, int]] = None):
         if n_blocks % world:
             raise ValueError(f"{n_blocks} blocks do not split evenly over {world} ranks")
         self.nb, self.world, self.L = n_blocks, world, block_len
@@ -66,14 +84,31 @@ class DistPlan:
         self.budgets = budget_table(n_blocks, budgets)
         self.layout = {e: EdgeLayout(n_kv_heads, min(b, block_len), head_dim, elem_bytes)
                        for e, b in self.budgets.items()}
-        # bytes from rank i to rank j: edges (s on i, r on j), ordered by (r, s)
+        self.help = dict(default_help(n_blocks, world) if help_sources is None else help_sources)
+        for r, k in self.help.items():
+            if not (0 <= k <= r) or self.helper(r) == self.owner(r) or self.n_local != 1:
+                raise ValueError(f"block {r}: cannot hand {k} sources to rank {self.helper(r)}")
+        # bytes from rank i to rank j: edges (s on i, consumed on j), ordered by (r, s)
         self.edges_ij = {(i, j): sorted(((s, r) for (s, r) in self.budgets if self.owner(s) == i
-                                         and self.owner(r) == j), key=lambda e: (e[1], e[0]))
+                                         and self.consumer((s, r)) == j), key=lambda e: (e[1], e[0]))
                          for i in range(world) for j in range(world)}
         self.bytes_ij = {ij: sum(self.layout[e].nbytes for e in es) for ij, es in self.edges_ij.items()}
 
     def owner(self, b: int) -> int:
         return block_owner(b, self.world)
+
+    def helper(self, r: int) -> int:
+        """Rank that takes part of block r's compact attention (its mirror's owner)."""
+        return self.owner(self.nb - 1 - r)
+
+    def consumer(self, e: Tuple[int, int]) -> int:
+        """Rank whose attention reads edge e = (s, r)."""
+        s, r = e
+        return self.helper(r) if s < self.help.get(r, 0) else self.owner(r)
+
+    def helped_by(self, rank: int) -> List[int]:
+        """Blocks of other ranks part of whose compact attention ``rank`` computes."""
+        return [r for r, k in sorted(self.help.items()) if k > 0 and self.helper(r) == rank]
 
     def local_index(self, b: int) -> int:
         return self.local_blocks(self.owner(b)).index(b)
@@ -103,7 +138,7 @@ class DistPlan:
         return out
 
     def recv_offsets(self, rank: int) -> Dict[Tuple[int, int], Tuple[str, int]]:
-        """Where each incoming edge (s -> r, r on rank) sits: ("recv"|"local", byte offset)."""
+        """Where each edge that rank consumes sits: ("recv"|"local", byte offset)."""
         out, off = {}, 0
         for i in range(self.world):
             if i == rank:
@@ -125,7 +160,11 @@ class DistributedDccKvLayer:
     def __init__(self, n_blocks: int, block_len: int, n_q_heads: int, n_kv_heads: int, head_dim: int,
                  budgets: Budgets, window: int, num_representative_queries: int = 64, projection_dim: int = 32,
                  lambda_beta: float = 1e-3, lambda_value: float = 1e-3, seed: int = 42,
-                 dtype: torch.dtype = torch.bfloat16, device=None, group=None):
+                 dtype: torch.dtype = torch.bfloat16, device=None, group=None,
+                 help_sources: Optional[Dict[int, int]] = None):
+        """``help_sources`` ({block: sources}) overrides the default hand-off
+        of compact attention from heavy blocks to their mirror's rank (see
+        ``default_help``; only with one block per rank)."""
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -139,7 +178,7 @@ class DistributedDccKvLayer:
         self.dtype = dtype
         self.code = L.dtype_code(torch.empty(0, dtype=dtype))
         self.plan = DistPlan(n_blocks, self.world, block_len, n_kv_heads, head_dim, budgets,
-                             torch.empty(0, dtype=dtype).element_size())
+                             torch.empty(0, dtype=dtype).element_size(), help_sources)
         self.n_local = self.plan.n_local
         self.local_blocks = self.plan.local_blocks(self.rank)
         dev = self.device
@@ -160,6 +199,18 @@ class DistributedDccKvLayer:
                         for e, loc in self.plan.send_offsets(self.rank).items()}
         self.o_loc = torch.empty(self.n_local, n_q_heads, block_len, head_dim, dtype=dtype, device=dev)
         self.lse_loc = torch.empty(self.n_local, n_q_heads, block_len, dtype=torch.float32, device=dev)
+        # compact attention handed between mirror ranks (one block per rank):
+        # a helped block's queries go to the helper, the helper's partial
+        # (O, LSE) over the handed sources comes back and is merged
+        self.helped = [r for r in self.local_blocks if self.plan.help.get(r, 0) > 0]
+        self.helping = self.plan.helped_by(self.rank)
+        qshape, lshape = (n_q_heads, block_len, head_dim), (n_q_heads, block_len)
+        self.q_help = {r: torch.empty(qshape, dtype=dtype, device=dev) for r in self.helping}
+        self.o_help = {r: torch.empty(qshape, dtype=dtype, device=dev) for r in self.helping}
+        self.lse_help = {r: torch.empty(lshape, dtype=torch.float32, device=dev) for r in self.helping}
+        self.o_from = {r: torch.empty(qshape, dtype=dtype, device=dev) for r in self.helped}
+        self.lse_from = {r: torch.empty(lshape, dtype=torch.float32, device=dev) for r in self.helped}
+        self.p2p_stream = torch.cuda.Stream(device=dev)
         # pooling, the gather, the builds and the exchange run on a high-priority
         # side stream, so their kernels are dispatched ahead of the local
         # attention that fills the GPU meanwhile on the main stream
@@ -193,7 +244,8 @@ class DistributedDccKvLayer:
             if len(self._bindings) >= 8:
                 self._bindings.pop(next(iter(self._bindings)))
             self._bindings[key] = bound
-        self.sets, self.build, self.local_problems, self.compact_problems, need = bound
+        (self.sets, self.build, self.local_problems, self.compact_problems, self.helper_problems, self.merges,
+         need) = bound
         if need > self._ws_bytes:
             # the workspace may still be in use by the side stream
             torch.cuda.current_stream(self.device).wait_stream(self.comm_stream)
@@ -224,16 +276,31 @@ class DistributedDccKvLayer:
         recv_off = self.plan.recv_offsets(self.rank)
         # the compact blocks continue each local block's online softmax from
         # its (O, LSE), in place: the merge needs no separate pass
-        compact_problems = []
-        for li, r in enumerate(self.local_blocks):
+        compact_problems, merges = [], []
+
+        def consumed_segments(r):
             segs = []
             for s in range(r):
+                if self.plan.consumer((s, r)) != self.rank:
+                    continue
                 buf, off = recv_off[(s, r)]
                 ko, vo, bo = self.plan.layout[(s, r)].views(self.bufs[buf], off, self.dtype)
                 segs.append(kv_segment(ko, vo, bo))
+            return segs
+
+        for li, r in enumerate(self.local_blocks):
+            segs = consumed_segments(r)
+            helped = r in self.helped
             if segs:
-                compact_problems.append(attn_problem(q[li], o[li], None, segs, o_init=o[li], lse_init=lse[li]))
-        return sets, build, local_problems, compact_problems, need
+                # a helped block also needs the LSE of its own part for the final merge
+                compact_problems.append(attn_problem(q[li], o[li], lse[li] if helped else None, segs,
+                                                     o_init=o[li], lse_init=lse[li]))
+            if helped:
+                merges.append((q[li], o[li], lse[li], r))
+        # this rank's part of other ranks' blocks: their queries over the handed sources
+        helper_problems = [attn_problem(self.q_help[r], self.o_help[r], self.lse_help[r], consumed_segments(r))
+                           for r in self.helping]
+        return sets, build, local_problems, compact_problems, helper_problems, merges, need
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
         """Local blocks q [n_local, H_q, L, d], k / v [n_local, H_kv, L, d] ->
@@ -261,6 +328,9 @@ class DistributedDccKvLayer:
         return self.o_loc
 
     __call__ = forward
+
+    def _peer(self, group_rank: int) -> int:
+        return group_rank if self.group is None else dist.get_global_rank(self.group, group_rank)
 
     def _attention(self, problems) -> None:
         dev = self.device
@@ -306,6 +376,21 @@ class DistributedDccKvLayer:
             ns, nr = sum(self.send_splits), sum(self.recv_splits)
             dist.all_to_all_single(self.recv_buf[:nr], self.send_buf[:ns], output_split_sizes=self.recv_splits,
                                    input_split_sizes=self.send_splits, group=self.group)
+        # helped blocks' queries to their helpers (after the collectives in
+        # issue order, on a stream that waits only for the inputs)
+        q_reqs = []
+        if self.helped or self.helping:
+            p2p = self.p2p_stream
+            p2p.wait_stream(main)  # inputs written, the previous helper attention done with q_help
+            if q_ready is not None:
+                for li in range(self.n_local):
+                    p2p.wait_event(q_ready[li])
+            ops = [dist.P2POp(dist.isend, q_send, self._peer(self.plan.helper(r)), self.group)
+                   for (q_send, _, _, r) in self.merges]
+            ops += [dist.P2POp(dist.irecv, self.q_help[r], self._peer(self.plan.owner(r)), self.group)
+                    for r in self.helping]
+            with torch.cuda.stream(p2p):
+                q_reqs = dist.batch_isend_irecv(ops)
         # local causal attention meanwhile, on the main stream
         if q_ready is None:
             self._attention(self.local_problems)
@@ -316,6 +401,26 @@ class DistributedDccKvLayer:
                 self._attention([self.local_problems[li]])
         main.wait_stream(side)
         run_attention(self.compact_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code, dev)
+        if self.helped or self.helping:
+            for req in q_reqs:
+                req.wait()  # the main stream waits for the query transfers
+            if self.helping:
+                run_attention(self.helper_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code,
+                              dev)
+            # partial states back to the helped blocks' ranks, merged there
+            ops = []
+            for r in self.helping:
+                dst = self._peer(self.plan.owner(r))
+                ops += [dist.P2POp(dist.isend, self.o_help[r], dst, self.group),
+                        dist.P2POp(dist.isend, self.lse_help[r], dst, self.group)]
+            for (_, _, _, r) in self.merges:
+                src = self._peer(self.plan.helper(r))
+                ops += [dist.P2POp(dist.irecv, self.o_from[r], src, self.group),
+                        dist.P2POp(dist.irecv, self.lse_from[r], src, self.group)]
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+            for (_, o_li, lse_li, r) in self.merges:
+                merge_lse([o_li, self.o_from[r]], [lse_li, self.lse_from[r]], out=o_li, want_lse=False)
         if done is not None:
             done.record(main)
         if merged is not None:
@@ -405,7 +510,7 @@ class DistributedDccKvLayer:
         sets = len(self.sets)
         pool = 0 if sets == 0 else 2 * -(-sets // 64)
         return (pool + build_launch_count(len(self.build), self.code, self.d) + -(-len(self.local_problems) // 8)
-                + -(-len(self.compact_problems) // 8))
+                + -(-len(self.compact_problems) // 8) + -(-len(self.helper_problems) // 8) + len(self.merges))
 
 
 class DistributedDccKvStack:

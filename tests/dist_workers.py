@@ -39,7 +39,7 @@ def exchange_worker(rank: int, world: int, port: int, n_blocks: int, budgets, er
         bufs["recv"] = recv
         for e, (buf, off) in plan.recv_offsets(rank).items():
             n = plan.layout[e].nbytes
-            assert plan.owner(e[1]) == rank
+            assert plan.consumer(e) == rank
             if not torch.equal(bufs[buf][off:off + n], _pattern(e, n)):
                 raise AssertionError(f"rank {rank}: edge {e} wrong at {buf}+{off}")
         dist.barrier()

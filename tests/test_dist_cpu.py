@@ -50,7 +50,7 @@ def test_plan_routes_every_edge_once(world):
             assert plan.owner(e[0]) == rank and e not in sent
             sent[e] = (rank, loc)
         for e, loc in plan.recv_offsets(rank).items():
-            assert plan.owner(e[1]) == rank and e not in received
+            assert plan.consumer(e) == rank and e not in received
             received[e] = (rank, loc)
         # byte ranges of one buffer never overlap
         for offsets in (plan.send_offsets(rank), plan.recv_offsets(rank)):
@@ -78,6 +78,27 @@ def test_snake_mapping_balances_compact_and_build_work(world):
     assert sorted(b for p in parts for b in p) == list(range(8))
     assert len({sum(p) for p in parts}) == 1
     assert len({sum(7 - b for b in p) for p in parts}) == 1
+
+
+def test_plan_hands_sources_of_heavy_blocks_to_their_mirror():
+    """One block per rank: block r > its mirror 7 - r hands its first
+    (r - (7 - r)) // 2 compact sources to the mirror's rank, which caps the
+    compact attention per rank at 4 of the 7 blocks of the last one."""
+    plan = DistPlan(8, 8, 16384, 8, 128, 1024)
+    assert plan.help == {7: 3, 6: 2, 5: 1}
+    load = [0] * 8
+    for (s, r) in plan.budgets:
+        load[plan.consumer((s, r))] += 1
+    assert max(load) == 4 and sum(load) == 28
+    assert plan.helped_by(0) == [7] and plan.helped_by(1) == [6] and plan.helped_by(7) == []
+    assert plan.consumer((2, 7)) == 0 and plan.consumer((3, 7)) == 7
+    # several blocks per rank: no hand-off; a forced one is refused
+    assert DistPlan(8, 4, 16384, 8, 128, 1024).help == {}
+    with pytest.raises(ValueError):
+        DistPlan(8, 4, 16384, 8, 128, 1024, help_sources={7: 2})
+    # a forced hand-off on two ranks (the 2-GPU test's setting)
+    plan2 = DistPlan(2, 2, 512, 2, 128, 64, help_sources={1: 1})
+    assert plan2.consumer((0, 1)) == 0 and plan2.helped_by(0) == [1]
 
 
 def test_plan_rejects_uneven_split():

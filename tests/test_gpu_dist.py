@@ -147,6 +147,73 @@ def test_layer_stack_double_buffered_exchange_matches_layer_by_layer(world):
     assert all(p.exitcode == 0 for p in procs)
 
 
+def _help_worker(rank, world, port, errq):
+    """One block per rank: part of the last blocks' compact attention is
+    computed on their mirror's rank and merged back."""
+    try:
+        import datetime
+        import torch.distributed as dist
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        import dcc_kv_b200 as dk
+        from dcc_kv_b200.dist_layer import DistributedDccKvLayer, local_blocks_of
+        from dcc_kv_b200.workloads import layer_inputs
+        nb = world
+        budgets = {(s, r): [64, 96, 128][(s + 2 * r) % 3] for r in range(nb) for s in range(r)}
+        help_sources = {1: 1} if world == 2 else None  # 4 ranks: the default hand-off {3: 1}
+        q, k, v = layer_inputs(nb, L, HQ, HKV, D, device="cpu", first_seed=13)
+        mine = local_blocks_of(nb, world, rank)
+        layer = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev, help_sources=help_sources)
+        assert layer.plan.help, "no hand-off configured"
+        out = None
+        for _ in range(2):
+            out = layer(q[mine].contiguous().to(dev), k[mine].contiguous().to(dev), v[mine].contiguous().to(dev))
+        torch.cuda.synchronize()
+        ref = dk.DccKvSyncLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev)(q.to(dev), k.to(dev), v.to(dev))
+        torch.cuda.synchronize()
+        for li, b in enumerate(mine):
+            err = ((out[li].float() - ref[b].float()).abs().max() / ref[b].float().abs().max()).item()
+            assert err < 2e-2, f"block {b}: {err}"
+        want = out.cpu()
+        hosts = tuple(t[mine].contiguous().pin_memory() for t in (q, k, v))
+        host_outs = [torch.empty(want.shape, dtype=want.dtype).pin_memory() for _ in range(2)]
+        for c in range(2):
+            layer(*hosts, out=host_outs[c])
+        torch.cuda.synchronize()
+        for c in range(2):
+            assert torch.equal(host_outs[c], want), c
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        errq.put(traceback.format_exc())
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_compact_attention_handed_to_mirror_rank(world):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = pymp.get_context("spawn")
+    errq = ctx.Queue()
+    port = random.randint(20000, 40000)
+    procs = [ctx.Process(target=_help_worker, args=(r, world, port, errq)) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=300)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not errors, "\n".join(errors)
+    assert all(p.exitcode == 0 for p in procs)
+
+
 def _ring_worker(rank, world, port, errq):
     try:
         import datetime
