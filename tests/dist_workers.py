@@ -42,6 +42,28 @@ def exchange_worker(rank: int, world: int, port: int, n_blocks: int, budgets, er
             assert plan.consumer(e) == rank
             if not torch.equal(bufs[buf][off:off + n], _pattern(e, n)):
                 raise AssertionError(f"rank {rank}: edge {e} wrong at {buf}+{off}")
+        # the compact-attention hand-off (one block per rank), in the layer's
+        # order: helped blocks' queries to their helpers, then each helper's
+        # partial state back to the helped block's rank
+        mine = plan.local_blocks(rank)
+        helped = [r for r in mine if plan.help.get(r, 0) > 0]
+        helping = plan.helped_by(rank)
+        q_in = {r: torch.zeros(64) for r in helping}
+        ops = [dist.P2POp(dist.isend, torch.full((64,), float(r)), plan.helper(r)) for r in helped]
+        ops += [dist.P2POp(dist.irecv, q_in[r], plan.owner(r)) for r in helping]
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        for r in helping:
+            assert torch.equal(q_in[r], torch.full((64,), float(r))), f"rank {rank}: queries of block {r}"
+        part_in = {r: torch.zeros(32) for r in helped}
+        ops = [dist.P2POp(dist.isend, torch.full((32,), 1000.0 + r), plan.owner(r)) for r in helping]
+        ops += [dist.P2POp(dist.irecv, part_in[r], plan.helper(r)) for r in helped]
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        for r in helped:
+            assert torch.equal(part_in[r], torch.full((32,), 1000.0 + r)), f"rank {rank}: partial of block {r}"
         dist.barrier()
         dist.destroy_process_group()
     except Exception:

@@ -116,8 +116,11 @@ def test_edge_layout_alignment():
         assert k.shape == (3, rows, 128) and b.shape == (3, rows)
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_gloo_exchange_by_plan(world):
+    """8 ranks: one block per rank, so the plan also hands compact sources of
+    blocks 5-7 to their mirrors' ranks (edge routing and the point-to-point
+    transfers of queries and partial states)."""
     budgets = {(s, r): [17, 64, 100][(s + r) % 3] for r in range(8) for s in range(r)}
     _spawn(dist_workers.exchange_worker, world, 8, budgets)
 
