@@ -21,7 +21,11 @@ blocks; round-robin would give 4 to 10).  One forward on every rank:
   4. compact attention with logit bias, one KV segment per source edge,
      read in place from the receive / local buffers, continuing each
      block's online softmax from the local (O, LSE) in place -- the merge
-     (online_softmax.py:92-111) happens inside that launch.
+     (online_softmax.py:92-111) happens inside that launch;
+  5. with one block per rank only (``default_help``): a heavy block's first
+     sources are consumed on its mirror block's rank -- its queries go there
+     once (point-to-point, after the collectives), that rank runs them over
+     the handed sources, and the partial (O, LSE) comes back and is merged.
 
 ``DistPlan`` is the pure host-side routing (offsets and split sizes),
 identical on every rank and testable without a GPU.
