@@ -272,12 +272,35 @@ def run_reference(args):
 # ---------------------------------------------------------------------------
 # GPU arm
 # ---------------------------------------------------------------------------
+_HOST_CPUS = None
+
+
+def bind_near_gpu(index: int) -> None:
+    """Run this process on the host cores nearest GPU ``index`` (NVML's
+    read-only CPU-affinity mask), so the pinned host buffers it allocates
+    afterwards sit in that socket's memory and the host <-> device copies
+    of the end-to-end leg do not cross the socket interconnect."""
+    global _HOST_CPUS
+    _HOST_CPUS = os.sched_getaffinity(0)
+    try:
+        nv, h = ClockSampler(index)._nvml_handle()
+        words = ((os.cpu_count() or 1) + 63) // 64
+        mask = nv.nvmlDeviceGetCpuAffinity(h, words)
+        cpus = {w * 64 + b for w, m in enumerate(mask) for b in range(64) if (int(m) >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        if cpus:
+            os.sched_setaffinity(0, cpus)
+    except Exception:
+        pass
+
+
 def _setup_dist():
     import datetime
     import torch.distributed as dist
     ws, rank, local = dist_env()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    bind_near_gpu(local)
     if ws > 1 and not dist.is_initialized():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
     return ws, rank, dev
@@ -398,7 +421,9 @@ def run_gpu(args):
         "clocks": clocks,
     }
     if args.cpu_baseline and ws == 1:
-        cores = os.cpu_count() or 1
+        if _HOST_CPUS:
+            os.sched_setaffinity(0, _HOST_CPUS)  # the CPU baseline uses every host core
+        cores = len(os.sched_getaffinity(0))
         torch.set_num_threads(cores)
         t, sample = cpu_sample()
         line["cpu_baseline"] = {"value": TOKENS / t, "unit": "tokens/s", "cores": cores, "kind": "port",
@@ -493,6 +518,44 @@ def exchange_study(args):
     _teardown(ws)
 
 
+def phase_study(args):
+    """Under torchrun (N >= 2): per rank, the mean time from the start of a
+    forward to the end of each phase (pooling, gather, builds, exchange on
+    the side stream; local attention, the wait for the exchange, compact
+    attention, hand-off transfers, helper attention, merge on the main
+    stream), CUDA events on each phase's stream.  One JSON line on rank 0
+    with every rank's figures; not the bench line."""
+    from dcc_kv_b200.dist_layer import DistributedDccKvLayer, local_blocks_of
+    from dcc_kv_b200.workloads import gqa_block
+    import torch.distributed as dist
+    ws, rank, dev = _setup_dist()
+    if ws < 2:
+        print(json.dumps({"study": "phase times", "unavailable": "needs 2+ GPUs under torchrun"}))
+        return
+    blocks = local_blocks_of(N_BLOCKS, ws, rank)
+    parts = [gqa_block(HQ, HKV, BLOCK_LEN, D, 1000 + b, device="cuda") for b in blocks]
+    q, k, v = (torch.stack([p_[i] for p_ in parts]) for i in range(3))
+    layer = DistributedDccKvLayer(N_BLOCKS, BLOCK_LEN, HQ, HKV, D, BUDGET, WINDOW, M_REPR, DP, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        layer(q, k, v)
+    _barrier(ws)
+    layer.phase_events = []
+    for _ in range(args.steps):
+        layer(q, k, v)
+    _barrier(ws)
+    mine = {"rank": rank, "blocks": blocks, "helped": layer.helped, "helping": layer.helping,
+            "build_problems": len(layer.build), "ms": layer.phase_times(layer.phase_events)}
+    layer.phase_events = None
+    everyone = [None] * ws
+    dist.all_gather_object(everyone, mine)
+    if rank == 0:
+        print(json.dumps({"study": "phase times", "n_gpus": ws, "steps": args.steps,
+                          "config": dict(WORKLOAD, parallelism=f"context parallel over {ws} GPUs"),
+                          "ranks": everyone}), flush=True)
+    del layer
+    _teardown(ws)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -509,9 +572,13 @@ def main():
                     help="under torchrun, N >= 2: time the compact exchange synchronous, overlapped, and "
                          "double buffered across --layers layers, and exit")
     ap.add_argument("--layers", type=int, default=4, help="layers in a row for --exchange-study")
+    ap.add_argument("--phase-times", action="store_true",
+                    help="under torchrun, N >= 2: per-rank times of each phase of the sharded layer, and exit")
     args = ap.parse_args()
     if args.exchange_study:
         exchange_study(args)
+    elif args.phase_times:
+        phase_study(args)
     elif args.profile_attention:
         profile_attention(args)
     elif args.impl == "reference":

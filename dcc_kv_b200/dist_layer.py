@@ -24,8 +24,9 @@ blocks; round-robin would give 4 to 10).  One forward on every rank:
      (online_softmax.py:92-111) happens inside that launch;
   5. with one block per rank only (``default_help``): a heavy block's first
      sources are consumed on its mirror block's rank -- its queries go there
-     once (point-to-point, after the collectives), that rank runs them over
-     the handed sources, and the partial (O, LSE) comes back and is merged.
+     once (point-to-point on a communicator of their own, so the transfer
+     waits only for the inputs), that rank runs them over the handed
+     sources, and the partial (O, LSE) comes back and is merged.
 
 ``DistPlan`` is the pure host-side routing (offsets and split sizes),
 identical on every rank and testable without a GPU.
@@ -165,10 +166,17 @@ class DistributedDccKvLayer:
                  budgets: Budgets, window: int, num_representative_queries: int = 64, projection_dim: int = 32,
                  lambda_beta: float = 1e-3, lambda_value: float = 1e-3, seed: int = 42,
                  dtype: torch.dtype = torch.bfloat16, device=None, group=None,
-                 help_sources: Optional[Dict[int, int]] = None):
+                 help_sources: Optional[Dict[int, int]] = None, p2p_group=None):
         """``help_sources`` ({block: sources}) overrides the default hand-off
         of compact attention from heavy blocks to their mirror's rank (see
-        ``default_help``; only with one block per rank)."""
+        ``default_help``; only with one block per rank).  The hand-off's
+        point-to-point transfers run on ``p2p_group``, a communicator of
+        their own with the ranks of ``group``: NCCL runs the operations of
+        one communicator in issue order on one internal stream, so on the
+        exchange's communicator the query transfer would queue behind the
+        all-to-allv, which waits for the builds.  By default every rank of
+        the default group creates it here (a collective call); with a
+        sub-``group``, pass it, else the transfers share ``group``."""
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -215,6 +223,15 @@ class DistributedDccKvLayer:
         self.o_from = {r: torch.empty(qshape, dtype=dtype, device=dev) for r in self.helped}
         self.lse_from = {r: torch.empty(lshape, dtype=torch.float32, device=dev) for r in self.helped}
         self.p2p_stream = torch.cuda.Stream(device=dev)
+        self.p2p_group = p2p_group
+        if self.plan.help and p2p_group is None:
+            if group is None:
+                self.p2p_group = dist.new_group(ranks=list(range(self.world)))
+                # the first operation on a communicator must involve all of
+                # its ranks; the hand-off transfers involve only some
+                dist.barrier(group=self.p2p_group)
+            else:
+                self.p2p_group = group
         # pooling, the gather, the builds and the exchange run on a high-priority
         # side stream, so their kernels are dispatched ahead of the local
         # attention that fills the GPU meanwhile on the main stream
@@ -230,6 +247,27 @@ class DistributedDccKvLayer:
         self._ws, self._ws_bytes = None, 0
         self.timing_events = None
         self.timing_index = 0
+        # optional list that collects, per forward, {phase: CUDA event}
+        # recorded on the stream that runs the phase (phase_times())
+        self.phase_events = None
+
+    def _mark(self, name: str, stream) -> None:
+        if self.phase_events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(stream)
+            self.phase_events[-1][name] = ev
+
+    @staticmethod
+    def phase_times(log) -> Dict[str, float]:
+        """Mean milliseconds from the start of a forward to each recorded
+        phase end, over the forwards in ``log`` (a ``phase_events`` list)."""
+        acc: Dict[str, float] = {}
+        for step in log:
+            t0 = step["start"]
+            for name, ev in step.items():
+                if name != "start":
+                    acc[name] = acc.get(name, 0.0) + t0.elapsed_time(ev) / len(log)
+        return acc
 
     def _bind(self, q, k, v, o=None, lse=None):
         """Point the kernel descriptors at q, k, v and the device output /
@@ -363,6 +401,9 @@ class DistributedDccKvLayer:
         dev = self.device
         main = torch.cuda.current_stream(dev)
         side = self.comm_stream if self.overlap_exchange else main
+        if self.phase_events is not None:
+            self.phase_events.append({})
+            self._mark("start", main)
         if side is not main:
             if side_waits is None:
                 side.wait_stream(main)  # inputs written, previous step's buffers released
@@ -373,13 +414,17 @@ class DistributedDccKvLayer:
             if windows_ready is not None:
                 side.wait_event(windows_ready)
             select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
+            self._mark("pooling", side)
             dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.group)
+            self._mark("gather", side)
             if kv_ready is not None:
                 side.wait_event(kv_ready)
             run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
+            self._mark("builds", side)
             ns, nr = sum(self.send_splits), sum(self.recv_splits)
             dist.all_to_all_single(self.recv_buf[:nr], self.send_buf[:ns], output_split_sizes=self.recv_splits,
                                    input_split_sizes=self.send_splits, group=self.group)
+            self._mark("exchange", side)
         # helped blocks' queries to their helpers (after the collectives in
         # issue order, on a stream that waits only for the inputs)
         q_reqs = []
@@ -389,12 +434,16 @@ class DistributedDccKvLayer:
             if q_ready is not None:
                 for li in range(self.n_local):
                     p2p.wait_event(q_ready[li])
-            ops = [dist.P2POp(dist.isend, q_send, self._peer(self.plan.helper(r)), self.group)
+            ops = [dist.P2POp(dist.isend, q_send, self._peer(self.plan.helper(r)), self.p2p_group)
                    for (q_send, _, _, r) in self.merges]
-            ops += [dist.P2POp(dist.irecv, self.q_help[r], self._peer(self.plan.owner(r)), self.group)
+            ops += [dist.P2POp(dist.irecv, self.q_help[r], self._peer(self.plan.owner(r)), self.p2p_group)
                     for r in self.helping]
             with torch.cuda.stream(p2p):
                 q_reqs = dist.batch_isend_irecv(ops)
+                if self.phase_events is not None:
+                    for req in q_reqs:
+                        req.wait()
+                    self._mark("query_handoff", p2p)
         # local causal attention meanwhile, on the main stream
         if q_ready is None:
             self._attention(self.local_problems)
@@ -403,28 +452,34 @@ class DistributedDccKvLayer:
             for li in range(self.n_local):
                 main.wait_event(q_ready[li])
                 self._attention([self.local_problems[li]])
+        self._mark("local_attention", main)
         main.wait_stream(side)
+        self._mark("exchange_wait", main)
         run_attention(self.compact_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code, dev)
+        self._mark("compact_attention", main)
         if self.helped or self.helping:
             for req in q_reqs:
                 req.wait()  # the main stream waits for the query transfers
             if self.helping:
                 run_attention(self.helper_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code,
                               dev)
+                self._mark("helper_attention", main)
             # partial states back to the helped blocks' ranks, merged there
             ops = []
             for r in self.helping:
                 dst = self._peer(self.plan.owner(r))
-                ops += [dist.P2POp(dist.isend, self.o_help[r], dst, self.group),
-                        dist.P2POp(dist.isend, self.lse_help[r], dst, self.group)]
+                ops += [dist.P2POp(dist.isend, self.o_help[r], dst, self.p2p_group),
+                        dist.P2POp(dist.isend, self.lse_help[r], dst, self.p2p_group)]
             for (_, _, _, r) in self.merges:
                 src = self._peer(self.plan.helper(r))
-                ops += [dist.P2POp(dist.irecv, self.o_from[r], src, self.group),
-                        dist.P2POp(dist.irecv, self.lse_from[r], src, self.group)]
+                ops += [dist.P2POp(dist.irecv, self.o_from[r], src, self.p2p_group),
+                        dist.P2POp(dist.irecv, self.lse_from[r], src, self.p2p_group)]
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
+            self._mark("partial_return", main)
             for (_, o_li, lse_li, r) in self.merges:
                 merge_lse([o_li, self.o_from[r]], [lse_li, self.lse_from[r]], out=o_li, want_lse=False)
+        self._mark("end", main)
         if done is not None:
             done.record(main)
         if merged is not None:

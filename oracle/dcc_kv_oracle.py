@@ -328,7 +328,7 @@ def layer_forward(q_blocks: List[np.ndarray], k_blocks: List[np.ndarray], v_bloc
         o_r = np.zeros((hq, len(sel), d))
         for h in range(hq):
             g = h // group
-            q = np.asarray(q_blocks[r][h], F64)[sel]
+            q = np.asarray(q_blocks[r][h][sel], F64)
             # local block, causal: row i sees keys [0, sel[i]]
             o_l, lse_l = attention_partial(q, k_blocks[r][g], v_blocks[r][g], positions=sel)
             state = (lse_l, np.ones_like(lse_l), o_l)

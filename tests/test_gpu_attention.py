@@ -179,3 +179,32 @@ def test_attention_continues_from_initial_state(dtype, hq, hkv, d):
     run_attention([prob], hq, hkv, d, 1.0 / d ** 0.5, L.dtype_code(qc), dev())
     torch.cuda.synchronize()
     assert torch.equal(o_in, o2) and torch.equal(l_in, l2)
+
+
+def test_merge_lse_cfg2_full_size():
+    """The merge microbenchmark at full size: 8 partial outputs
+    [32, 4096, 128] bf16 with fp32 LSE ~ N(0,1)*4.  The whole output against
+    the LSE-weighted sum in fp32 (torch, on the device) and 64 sampled
+    (head, query) rows against the FP64 oracle fold of
+    online_softmax.py:92-111; bf16 output within 2e-2 relative (it lands
+    at bf16 rounding), LSE within 1e-5."""
+    from dcc_kv_b200.workloads import merge_inputs
+    outs, lses = merge_inputs(8, 32, 4096, 128, seed=0, device="cuda")
+    o, lse = dk.merge_lse(outs, lses)
+    torch.cuda.synchronize()
+    ls = torch.stack(lses)                       # [8, 32, 4096]
+    m = ls.max(dim=0).values
+    w = torch.exp(ls - m)
+    want = (w[..., None] * torch.stack([x.float() for x in outs])).sum(0) / w.sum(0)[..., None]
+    want_lse = m + torch.log(w.sum(0))
+    err = ((o.float() - want).abs().max() / want.abs().max()).item()
+    assert err < 2e-2, err
+    assert ((lse - want_lse).abs().max() / want_lse.abs().max()).item() < 1e-5
+    g = torch.Generator().manual_seed(9)
+    hs = torch.randint(0, 32, (64,), generator=g)
+    qs = torch.randint(0, 4096, (64,), generator=g)
+    ro = [x[hs, qs].double().cpu().numpy() for x in outs]
+    rl = [x[hs, qs].double().cpu().numpy() for x in lses]
+    want_o, want_l = orc.merge_lse(ro, rl)
+    assert rel_err(np64(o[hs, qs]), want_o) < 2e-2
+    assert rel_err(np64(lse[hs, qs]), want_l) < 1e-5

@@ -1,9 +1,18 @@
-"""The sharded layer on 2+ GPUs (one process per GPU, NCCL) against the
-single-GPU layer on the same inputs: every rank's blocks agree within the
-bf16 bar (2e-2); the two differ only in how the compact blocks are split
-into KV tiles.  The host-buffer call must reproduce the device call bit for
-bit.  The single-rank case runs the same code on one GPU; the others are
-skipped on a box with fewer GPUs."""
+"""The sharded layer on 1, 2, 4 and 8 GPUs (one process per GPU, NCCL).
+
+* every rank's blocks against the FP64 oracle (each rank recomputes its own
+  blocks: every edge into them, all KV heads, all rows) within the bf16 bar
+  2e-2, and against the single-GPU layer on the same inputs;
+* with one block per rank (world = blocks), the default hand-off of compact
+  attention to the mirror block's rank: against the oracle, and against the
+  same layer without a hand-off within a few bf16 rounding steps (the two
+  differ by one LSE merge of bf16 partials), so a dropped or doubled source
+  would show;
+* the host-buffer call reproduces the device call bit for bit;
+* the double-buffered layer stack equals layer-by-layer calls bit for bit,
+  with and without a hand-off.
+
+Cases needing more GPUs than the box has are skipped."""
 from __future__ import annotations
 
 import multiprocessing as pymp
@@ -11,46 +20,100 @@ import os
 import random
 import traceback
 
+import numpy as np
 import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
 
 NB, L, HQ, HKV, D = 4, 512, 8, 2, 128
-BUDGETS = {(s, r): [64, 96, 128][(s + 2 * r) % 3] for r in range(NB) for s in range(r)}
 
 
-def _worker(rank, world, port, errq):
+def _budgets(nb):
+    return {(s, r): [64, 96, 128][(s + 2 * r) % 3] for r in range(nb) for s in range(r)}
+
+
+BUDGETS = _budgets(NB)
+
+
+def _init(rank, world, port):
+    import datetime
+    import torch.distributed as dist
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dev = torch.device("cuda", rank)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=dev)
+    return dist, dev
+
+
+def _spawn(target, world, *args):
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    ctx = pymp.get_context("spawn")
+    errq = ctx.Queue()
+    port = random.randint(20000, 40000)
+    procs = [ctx.Process(target=target, args=(r, world, port, errq) + args) for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=420)
+    for p in procs:
+        if p.is_alive():
+            p.kill()
+    errors = []
+    while not errq.empty():
+        errors.append(errq.get())
+    assert not errors, "\n".join(errors)
+    assert all(p.exitcode == 0 for p in procs)
+
+
+def _oracle_blocks(q, k, v, budgets, window, blocks):
+    """FP64 oracle output of ``blocks`` (all heads, all rows): every edge
+    into them is built (dcc_kv_sync_cpu.py:52-84, compact_kv.py:50-118)."""
+    from oracle import dcc_kv_oracle as orc
+    top = max(blocks) + 1
+    ref, _ = orc.layer_forward([x.float().numpy() for x in q[:top]], [x.float().numpy() for x in k[:top]],
+                               [x.float().numpy() for x in v[:top]],
+                               {(s, r): budgets[(s, r)] for r in range(top) for s in range(r)}, window,
+                               rows={b: np.array([0]) for b in range(top) if b not in blocks})
+    return {b: ref[b] for b in blocks}
+
+
+def _rel(got, want):
+    got = got.double().cpu().numpy() if isinstance(got, torch.Tensor) else got
+    return float(np.abs(got - want).max() / np.abs(want).max())
+
+
+def _worker(rank, world, port, errq, nb):
     try:
-        import datetime
-        import torch.distributed as dist
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
-        dev = torch.device("cuda", rank)
-        torch.cuda.set_device(dev)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist, dev = _init(rank, world, port)
         import dcc_kv_b200 as dk
-        from dcc_kv_b200.dist_layer import DistributedDccKvLayer
+        from dcc_kv_b200.dist_layer import DistributedDccKvLayer, local_blocks_of
         from dcc_kv_b200.workloads import layer_inputs
-        q, k, v = layer_inputs(NB, L, HQ, HKV, D, device="cpu", first_seed=11)
-        from dcc_kv_b200.dist_layer import local_blocks_of
-        mine = local_blocks_of(NB, world, rank)
-        layer = DistributedDccKvLayer(NB, L, HQ, HKV, D, BUDGETS, window=128, device=dev)
+        budgets = _budgets(nb)
+        q, k, v = layer_inputs(nb, L, HQ, HKV, D, device="cpu", first_seed=11)
+        mine = local_blocks_of(nb, world, rank)
+        layer = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev)
         out = None
         for _ in range(2):  # second call reuses every buffer
             out = layer(q[mine].contiguous().to(dev), k[mine].contiguous().to(dev), v[mine].contiguous().to(dev))
         torch.cuda.synchronize()
-        ref = dk.DccKvSyncLayer(NB, L, HQ, HKV, D, BUDGETS, window=128, device=dev)(q.to(dev), k.to(dev), v.to(dev))
+        from gpu_util import assert_no_device_timeouts
+        assert_no_device_timeouts()
+        ref = dk.DccKvSyncLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev)(q.to(dev), k.to(dev), v.to(dev))
         torch.cuda.synchronize()
+        want = _oracle_blocks(q, k, v, budgets, 128, mine)
         for li, b in enumerate(mine):
+            assert _rel(out[li], want[b]) < 2e-2, f"block {b} vs oracle"
             err = ((out[li].float() - ref[b].float()).abs().max() / ref[b].float().abs().max()).item()
             assert err < 2e-2, f"block {b}: {err}"
         # host buffers: copies pipelined with the compute, same kernels, same
         # result; three calls alternating two inputs (consecutive calls use
         # alternate device staging sets and overlap one another)
         want = [out.cpu()]
-        q2, k2, v2 = layer_inputs(NB, L, HQ, HKV, D, device="cpu", first_seed=29)
+        q2, k2, v2 = layer_inputs(nb, L, HQ, HKV, D, device="cpu", first_seed=29)
         want.append(layer(q2[mine].contiguous().to(dev), k2[mine].contiguous().to(dev),
                           v2[mine].contiguous().to(dev)).cpu())
         hosts = [tuple(t[mine].contiguous().pin_memory() for t in x) for x in ((q, k, v), (q2, k2, v2))]
@@ -61,123 +124,101 @@ def _worker(rank, world, port, errq):
         for c in range(3):
             assert torch.equal(host_outs[c], want[c % 2]), c
         dist.barrier()
+        del layer
         dist.destroy_process_group()
     except Exception:
         errq.put(traceback.format_exc())
 
 
-@pytest.mark.parametrize("world", [1, 2])
-def test_distributed_layer_matches_single_gpu(world):
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
-    ctx = pymp.get_context("spawn")
-    errq = ctx.Queue()
-    port = random.randint(20000, 40000)
-    procs = [ctx.Process(target=_worker, args=(r, world, port, errq)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    errors = []
-    while not errq.empty():
-        errors.append(errq.get())
-    assert not errors, "\n".join(errors)
-    assert all(p.exitcode == 0 for p in procs)
+@pytest.mark.parametrize("world", [1, 2, 4])
+def test_distributed_layer_matches_oracle_and_single_gpu(world):
+    """4 blocks on 1, 2 or 4 ranks (4 ranks: one block per rank, so the
+    default hand-off {3: 1} is on)."""
+    _spawn(_worker, world, NB)
 
 
-def _stack_worker(rank, world, port, errq):
+def test_distributed_layer_8_ranks_default_handoff():
+    """8 blocks on 8 ranks: the default hand-off {7: 3, 6: 2, 5: 1}."""
+    _spawn(_worker, 8, 8)
+
+
+def _stack_worker(rank, world, port, errq, nb, help_sources):
     try:
-        import datetime
-        import torch.distributed as dist
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
-        dev = torch.device("cuda", rank)
-        torch.cuda.set_device(dev)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist, dev = _init(rank, world, port)
         from dcc_kv_b200.dist_layer import DistributedDccKvLayer, DistributedDccKvStack
         from dcc_kv_b200.workloads import layer_inputs
         from dcc_kv_b200.dist_layer import local_blocks_of
-        mine = local_blocks_of(NB, world, rank)
+        budgets = _budgets(nb)
+        mine = local_blocks_of(nb, world, rank)
         inputs = []
         for seed in (11, 29, 47):
-            q, k, v = layer_inputs(NB, L, HQ, HKV, D, device="cpu", first_seed=seed)
+            q, k, v = layer_inputs(nb, L, HQ, HKV, D, device="cpu", first_seed=seed)
             inputs.append(tuple(t[mine].contiguous().to(dev) for t in (q, k, v)))
-        layer = DistributedDccKvLayer(NB, L, HQ, HKV, D, BUDGETS, window=128, device=dev)
+        kw = dict(window=128, device=dev, help_sources=help_sources)
+        layer = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, **kw)
+        assert bool(layer.plan.help) == bool(help_sources)
         want = [layer(*x).clone() for x in inputs]
         # no communication-computation overlap: same kernels, same outputs
         layer.overlap_exchange = False
         for x, w in zip(inputs, want):
             assert torch.equal(layer(*x), w)
         # exchange of layer l + 1 overlapped with the attention of layer l
-        stack = DistributedDccKvStack(NB, L, HQ, HKV, D, BUDGETS, window=128, device=dev)
+        stack = DistributedDccKvStack(nb, L, HQ, HKV, D, budgets, **kw)
         for _ in range(2):  # second call reuses every buffer
             outs = stack(inputs)
             torch.cuda.synchronize()
             for li, (o, w) in enumerate(zip(outs, want)):
                 assert torch.equal(o, w), f"layer {li}"
         dist.barrier()
+        del stack, layer
         dist.destroy_process_group()
     except Exception:
         errq.put(traceback.format_exc())
 
 
-@pytest.mark.parametrize("world", [1, 2])
-def test_layer_stack_double_buffered_exchange_matches_layer_by_layer(world):
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
-    ctx = pymp.get_context("spawn")
-    errq = ctx.Queue()
-    port = random.randint(20000, 40000)
-    procs = [ctx.Process(target=_stack_worker, args=(r, world, port, errq)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    errors = []
-    while not errq.empty():
-        errors.append(errq.get())
-    assert not errors, "\n".join(errors)
-    assert all(p.exitcode == 0 for p in procs)
+@pytest.mark.parametrize("world,nb,help_sources", [(1, NB, None), (2, NB, None), (2, 2, {1: 1}),
+                                                   (4, NB, {3: 1})])
+def test_layer_stack_double_buffered_exchange_matches_layer_by_layer(world, nb, help_sources):
+    """Two layer slots, each with its own exchange buffers, hand-off buffers,
+    point-to-point stream and communicator, interleaved layer by layer."""
+    _spawn(_stack_worker, world, nb, help_sources)
 
 
 def _help_worker(rank, world, port, errq):
     """One block per rank: part of the last blocks' compact attention is
     computed on their mirror's rank and merged back."""
     try:
-        import datetime
-        import torch.distributed as dist
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
-        dev = torch.device("cuda", rank)
-        torch.cuda.set_device(dev)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
-        import dcc_kv_b200 as dk
+        dist, dev = _init(rank, world, port)
         from dcc_kv_b200.dist_layer import DistributedDccKvLayer, local_blocks_of
         from dcc_kv_b200.workloads import layer_inputs
         nb = world
-        budgets = {(s, r): [64, 96, 128][(s + 2 * r) % 3] for r in range(nb) for s in range(r)}
-        help_sources = {1: 1} if world == 2 else None  # 4 ranks: the default hand-off {3: 1}
+        budgets = _budgets(nb)
+        help_sources = {1: 1} if world == 2 else None  # 4 / 8 ranks: the default hand-off
         q, k, v = layer_inputs(nb, L, HQ, HKV, D, device="cpu", first_seed=13)
         mine = local_blocks_of(nb, world, rank)
+        xs = [t[mine].contiguous().to(dev) for t in (q, k, v)]
         layer = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev, help_sources=help_sources)
         assert layer.plan.help, "no hand-off configured"
         out = None
         for _ in range(2):
-            out = layer(q[mine].contiguous().to(dev), k[mine].contiguous().to(dev), v[mine].contiguous().to(dev))
+            out = layer(*xs)
         torch.cuda.synchronize()
-        ref = dk.DccKvSyncLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev)(q.to(dev), k.to(dev), v.to(dev))
+        plain = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev, help_sources={})
+        out0 = plain(*xs)
         torch.cuda.synchronize()
+        from gpu_util import assert_no_device_timeouts
+        assert_no_device_timeouts()
+        want = _oracle_blocks(q, k, v, budgets, 128, mine)
         for li, b in enumerate(mine):
-            err = ((out[li].float() - ref[b].float()).abs().max() / ref[b].float().abs().max()).item()
-            assert err < 2e-2, f"block {b}: {err}"
+            assert _rel(out[li], want[b]) < 2e-2, f"block {b} vs oracle"
+            if b in layer.plan.help:
+                # the hand-off adds one LSE merge of two bf16-rounded partials:
+                # a few bf16 rounding steps (2^-9 relative each); a dropped or
+                # doubled compact source moves the output by far more
+                err = ((out[li].float() - out0[li].float()).abs().max() / out0[li].float().abs().max()).item()
+                assert err < 1e-2, f"block {b}: {err}"
+            else:
+                assert torch.equal(out[li], out0[li]), f"block {b}: changed by the hand-off"
         want = out.cpu()
         hosts = tuple(t[mine].contiguous().pin_memory() for t in (q, k, v))
         host_outs = [torch.empty(want.shape, dtype=want.dtype).pin_memory() for _ in range(2)]
@@ -187,43 +228,20 @@ def _help_worker(rank, world, port, errq):
         for c in range(2):
             assert torch.equal(host_outs[c], want), c
         dist.barrier()
+        del layer, plain
         dist.destroy_process_group()
     except Exception:
         errq.put(traceback.format_exc())
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_compact_attention_handed_to_mirror_rank(world):
-    if torch.cuda.device_count() < world:
-        pytest.skip(f"needs {world} GPUs")
-    ctx = pymp.get_context("spawn")
-    errq = ctx.Queue()
-    port = random.randint(20000, 40000)
-    procs = [ctx.Process(target=_help_worker, args=(r, world, port, errq)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    errors = []
-    while not errq.empty():
-        errors.append(errq.get())
-    assert not errors, "\n".join(errors)
-    assert all(p.exitcode == 0 for p in procs)
+    _spawn(_help_worker, world)
 
 
 def _ring_worker(rank, world, port, errq):
     try:
-        import datetime
-        import torch.distributed as dist
-        os.environ["MASTER_ADDR"] = "127.0.0.1"
-        os.environ["MASTER_PORT"] = str(port)
-        dev = torch.device("cuda", rank)
-        torch.cuda.set_device(dev)
-        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                                device_id=dev)
+        dist, dev = _init(rank, world, port)
         from dcc_kv_b200 import baselines as bl
         g = torch.Generator().manual_seed(5)
         T, d = 256 * world, 128
@@ -242,22 +260,6 @@ def _ring_worker(rank, world, port, errq):
         errq.put(traceback.format_exc())
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ring_attention_over_nccl_matches_single_gpu():
-    world = 2
-    ctx = pymp.get_context("spawn")
-    errq = ctx.Queue()
-    port = random.randint(20000, 40000)
-    procs = [ctx.Process(target=_ring_worker, args=(r, world, port, errq)) for r in range(world)]
-    for p in procs:
-        p.start()
-    for p in procs:
-        p.join(timeout=300)
-    for p in procs:
-        if p.is_alive():
-            p.kill()
-    errors = []
-    while not errq.empty():
-        errors.append(errq.get())
-    assert not errors, "\n".join(errors)
-    assert all(p.exitcode == 0 for p in procs)
+@pytest.mark.parametrize("world", [2, 8])
+def test_ring_attention_over_nccl_matches_single_gpu(world):
+    _spawn(_ring_worker, world)

@@ -6,8 +6,9 @@ compact attention with logit bias + online-softmax merge).
 * config 1 (K,V [4096,128], Q [512,128], budget 64, local block 512): golden
   merged output, float32 within 1e-4;
 * bf16 layer at reduced size against the FP64 oracle within 2e-2;
-* full 128K layer (8 x 16384, 32/8 heads, budget 1024, bf16): sampled query
-  rows of every block against the oracle within 2e-2.
+* full 128K layer (8 x 16384, 32/8 heads, budget 1024, bf16) and the 1M
+  layer with variable budgets: sampled query rows of every block against
+  the oracle within 2e-2.
 """
 from __future__ import annotations
 
@@ -63,9 +64,11 @@ def test_cfg1_two_block_merge_golden_f32():
 
 
 def _oracle_layer(q, k, v, budgets, window, M, dp, rows=None):
-    qb = [x.double().numpy() for x in q]
-    kb = [x.double().numpy() for x in k]
-    vb = [x.double().numpy() for x in v]
+    # float32 holds bf16 / float32 inputs exactly; the oracle widens each
+    # head to FP64 as it reads it (a 1M-token block in FP64 would be GBs)
+    qb = [x.float().numpy() for x in q]
+    kb = [x.float().numpy() for x in k]
+    vb = [x.float().numpy() for x in v]
     return orc.layer_forward(qb, kb, vb, budgets, window, M, dp, rows=rows)
 
 
@@ -85,8 +88,19 @@ def test_layer_bf16_small(schedule):
         assert rel_err(np64(out[r]), ref[r]) < 2e-2, r
 
 
+def _kv_head_slice(q, k, v, g, group):
+    """The layer is independent across KV heads: KV head g with its query
+    heads g*group .. (g+1)*group-1, every block."""
+    return q[:, g * group:(g + 1) * group].cpu(), k[:, g:g + 1].cpu(), v[:, g:g + 1].cpu()
+
+
 @pytest.mark.slow
-def test_layer_full_128k_bf16_sampled():
+def test_layer_full_128k_bf16_all_blocks_sampled():
+    """The benchmarked layer (8 x 16384, 32/8 heads, budget 1024, window
+    2048): sampled query rows of every block -- block 7 with its seven
+    compact sources included -- for KV heads 0 and 5 (their query heads
+    0-3 and 20-23) against the FP64 oracle, which builds every edge into
+    each block for that head (dcc_kv_sync_cpu.py:52-84)."""
     from dcc_kv_b200.workloads import layer_inputs
     nb, L, hq, hkv, d = 8, 16384, 32, 8, 128
     q, k, v = layer_inputs(nb, L, hq, hkv, d, device="cpu")
@@ -94,15 +108,16 @@ def test_layer_full_128k_bf16_sampled():
     out = layer(q.to(dev()), k.to(dev()), v.to(dev()))
     torch.cuda.synchronize()
     assert_no_device_timeouts()
-    rows = {b: np.array([0, 1, 777, 8191, 16383]) for b in range(nb)}
-    # oracle over three blocks (building every edge into them), sampled rows
-    sub = [0, 1, 2]
-    ref, _ = _oracle_layer(q[sub], k[sub], v[sub], {(s, r): 1024 for r in range(3) for s in range(r)}, 2048, 64, 32,
-                           rows=rows)
-    for r in sub:
-        got = np64(out[r][:, rows[r]])
-        assert rel_err(got, ref[r]) < 2e-2, r
     assert torch.isfinite(out).all()
+    rows = {b: np.array([0, 1, 777, 2047, 2048, 8191, 12345, L - 1]) for b in range(nb)}
+    budgets = {(s, r): 1024 for r in range(nb) for s in range(r)}
+    group = hq // hkv
+    for g in (0, 5):
+        qh, kh, vh = _kv_head_slice(q, k, v, g, group)
+        ref, _ = _oracle_layer(qh, kh, vh, budgets, 2048, 64, 32, rows=rows)
+        for r in range(nb):
+            got = np64(out[r, g * group:(g + 1) * group][:, rows[r]])
+            assert rel_err(got, ref[r]) < 2e-2, (g, r)
 
 
 def test_layer_host_buffers_match_device_path():
@@ -135,11 +150,11 @@ def test_layer_host_buffers_match_device_path():
 
 
 @pytest.mark.slow
-def test_layer_1m_variable_budgets_sampled():
+def test_layer_1m_variable_budgets_all_blocks_sampled():
     """1M-token layer (8 x 131072, 32/8 heads, window 2048, budgets drawn from
-    {256, 512, 1024, 2048} with seed 1): the whole layer runs on the GPU; KV
-    head 0 (query heads 0-3) of blocks 0-2 is recomputed by the oracle on
-    sampled rows (the layer is independent across KV heads)."""
+    {256, 512, 1024, 2048} with seed 1): the whole layer runs on the GPU;
+    sampled rows of every block for KV head 3 (query heads 12-15) are
+    recomputed by the oracle, which builds all 28 edges of that head."""
     from dcc_kv_b200.workloads import layer_inputs, variable_budgets
     nb, L, hq, hkv, d = 8, 131072, 32, 8, 128
     budgets = variable_budgets(nb)
@@ -149,12 +164,10 @@ def test_layer_1m_variable_budgets_sampled():
     torch.cuda.synchronize()
     assert_no_device_timeouts()
     assert torch.isfinite(out).all()
-    sub = [0, 1, 2]
-    rows = {b: np.array([0, 1, 2047, 2048, 77777, L - 1]) for b in sub}
-    qh = q[sub, 0:4].cpu()
-    kh, vh = k[sub, 0:1].cpu(), v[sub, 0:1].cpu()
-    ref, _ = _oracle_layer(qh, kh, vh, {(s, r): budgets[(s, r)] for r in sub for s in range(r)}, 2048, 64, 32,
-                           rows=rows)
-    for r in sub:
-        got = np64(out[r, 0:4][:, rows[r]])
+    group, g = hq // hkv, 3
+    rows = {b: np.array([0, 1, 2047, 2048, 77777, L - 1]) for b in range(nb)}
+    qh, kh, vh = _kv_head_slice(q, k, v, g, group)
+    ref, _ = _oracle_layer(qh, kh, vh, budgets, 2048, 64, 32, rows=rows)
+    for r in range(nb):
+        got = np64(out[r, g * group:(g + 1) * group][:, rows[r]])
         assert rel_err(got, ref[r]) < 2e-2, r
