@@ -107,6 +107,8 @@ SIGNATURES = {
     "dcc_attention_fwd": (_I, [_P, _I, _I, _I, _I, _D, _I, _P]),
     "dcc_device_error_status": (_I, [_I]),
     "dcc_build_error_status": (_I, [_I]),
+    "dcc_device_error_flags_async": (_I, [_P, _P]),
+    "dcc_debug_expire_wait": (_I, [C.c_uint64, _P]),
     "dcc_online_softmax_from_attention": (_I, [_P, _P, _P, _I64, _I64, _I64, _I64, _I, _P, _P, _P, _P]),
     "dcc_merge_softmax_states": (_I, [_P, _P, _P, _P, _P, _P, _I64, _I64, _I, _P, _P, _P, _P]),
     "dcc_merge_lse": (_I, [_P, _P, _I, _I64, _I64, _I, _P, _P, _P]),
@@ -168,3 +170,42 @@ def ptr(t: Optional[torch.Tensor]) -> Optional[int]:
 def workspace(nbytes: int, device: torch.device) -> torch.Tensor:
     """A caller-owned scratch buffer (the library itself never allocates)."""
     return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+class DeviceErrorWatch:
+    """Bounded device-side waits that gave up, seen from the host without a
+    synchronisation.  The tcgen05 kernels never hang: a wait that passes its
+    limit records a flag and the kernel unwinds, leaving its outputs
+    unusable.  ``record`` enqueues an asynchronous copy of the library's two
+    flags (attention, scoring) into a pinned host pair at the end of a
+    forward; ``poll`` raises ``DccError(DCC_ERR_TIMEOUT)`` when the copy
+    that has landed shows a flag, so a forward whose kernel gave up is
+    reported by the next call.  ``check`` synchronises the device first."""
+
+    def __init__(self):
+        self.host: Optional[torch.Tensor] = None
+
+    def record(self, stream: torch.cuda.Stream) -> None:
+        if self.host is None:
+            self.host = torch.zeros(2, dtype=torch.int32).pin_memory()
+        check(lib().dcc_device_error_flags_async(self.host.data_ptr(), stream.cuda_stream),
+              "device_error_flags_async")
+
+    def poll(self) -> None:
+        if self.host is None:
+            return
+        a, s = (int(x) for x in self.host.tolist())
+        if a or s:
+            self.host.zero_()
+            # clears the device words (this synchronises; only on the error path)
+            lib().dcc_device_error_status(1)
+            lib().dcc_build_error_status(1)
+            raise DccError(DCC_ERR_TIMEOUT,
+                           f"a bounded device wait expired in an earlier forward (attention flags {a}, "
+                           f"scoring flags {s}); its output is not valid")
+
+    def check(self, device: torch.device) -> None:
+        torch.cuda.synchronize(device)
+        self.poll()
+        check(lib().dcc_device_error_status(1), "attention")
+        check(lib().dcc_build_error_status(1), "compact-KV build")

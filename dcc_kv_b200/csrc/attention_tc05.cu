@@ -24,6 +24,7 @@
 // Every mbarrier wait is bounded (2 s); a timeout sets g_attn_error, the
 // roles unwind, in-flight copies and MMAs are waited for, TMEM is freed.
 #include <memory>
+#include <mutex>
 #include <string>
 
 #include "attention.cuh"
@@ -115,6 +116,9 @@ __device__ __forceinline__ uint64_t vdesc(const unsigned char* tile, int kk) {
 // warp-collective tcgen05 instruction while another has given up.
 __device__ __forceinline__ bool warp_wait(uint64_t* bar, uint32_t parity) {
   return __all_sync(0xffffffffu, mbar_wait(bar, parity)) != 0;
+}
+__device__ __forceinline__ bool warp_wait_limited(uint64_t* bar, uint32_t parity, uint64_t limit_ns) {
+  return __all_sync(0xffffffffu, mbar_wait(bar, parity, limit_ns)) != 0;
 }
 
 // 2^x on the SFU (ex2.approx.ftz: ~2 ulp, 2^-inf = 0).
@@ -602,9 +606,60 @@ bool attn_tc05_supported(const dcc_attn_problem& p, const AttnParams& prm) {
   return true;
 }
 
+int score_error_flag_address(unsigned int** out);
+
+// Both error words to host memory by a posted write from the device (pinned
+// host memory is device-accessible under unified addressing), so reading
+// them needs neither a copy engine nor a synchronisation.
+__global__ void flags_to_host_kernel(const unsigned int* score_flag, unsigned int* host) {
+  host[0] = *reinterpret_cast<volatile unsigned int*>(&g_attn_error);
+  host[1] = *reinterpret_cast<const volatile unsigned int*>(score_flag);
+  __threadfence_system();
+}
+
+// One warp waits, with the same bounded wait as the kernels above, on an
+// mbarrier that nothing arrives at; when the limit passes it records the
+// timeout in the attention error word (bit 16).  It has no asynchronous
+// copy or MMA in flight, so it simply returns.
+__global__ void expire_wait_kernel(uint64_t limit_ns) {
+  __shared__ uint64_t bar;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (!warp_wait_limited(&bar, 0, limit_ns) && threadIdx.x == 0) atomicOr(&g_attn_error, 16u);
+}
+
 }  // namespace dcc
 
 using namespace dcc;
+
+extern "C" int dcc_device_error_flags_async(unsigned int* host_flags, void* stream) {
+  if (host_flags == nullptr) return fail(DCC_ERR_INVALID_ARGUMENT, "device_error_flags_async: null destination");
+  static std::mutex mu;
+  static unsigned int* score_flag[64] = {};
+  int dev = 0;
+  DCC_CHECK(check_cuda(cudaGetDevice(&dev), "device_error_flags_async: cudaGetDevice"));
+  if (dev < 0 || dev >= 64) return fail(DCC_ERR_UNSUPPORTED, "device_error_flags_async: device ordinal above 63");
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (score_flag[dev] == nullptr) DCC_CHECK(score_error_flag_address(&score_flag[dev]));
+  }
+  cudaPointerAttributes pa{};
+  DCC_CHECK(check_cuda(cudaPointerGetAttributes(&pa, host_flags), "device_error_flags_async: pointer attributes"));
+  if (pa.type != cudaMemoryTypeHost || pa.devicePointer == nullptr)
+    return fail(DCC_ERR_INVALID_ARGUMENT, "device_error_flags_async: destination must be pinned host memory");
+  flags_to_host_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(
+      score_flag[dev], static_cast<unsigned int*>(pa.devicePointer));
+  return check_cuda(cudaGetLastError(), "device_error_flags_async launch");
+}
+
+extern "C" int dcc_debug_expire_wait(uint64_t limit_ns, void* stream) {
+  if (limit_ns > 100000000ull) return fail(DCC_ERR_INVALID_ARGUMENT, "debug_expire_wait: limit above 100 ms");
+  expire_wait_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns);
+  return check_cuda(cudaGetLastError(), "debug_expire_wait launch");
+}
 
 extern "C" int dcc_device_error_status(int clear) {
   DCC_CHECK(check_cuda(cudaDeviceSynchronize(), "device_error_status: synchronize"));

@@ -511,6 +511,13 @@ int launch_scoring_tc05(const BuildBatch<float>& bb, const BuildParams& prm, int
   return DCC_OK;
 }
 
+// Device address of the scoring passes' bounded-wait error word on the
+// current device (the symbol lives in this translation unit).
+int score_error_flag_address(unsigned int** out) {
+  return check_cuda(cudaGetSymbolAddress(reinterpret_cast<void**>(out), g_score_error),
+                    "device_error_flags_async: scoring flag address");
+}
+
 }  // namespace dcc
 
 extern "C" int dcc_build_error_status(int clear) {

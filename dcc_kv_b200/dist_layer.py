@@ -250,6 +250,7 @@ class DistributedDccKvLayer:
         # optional list that collects, per forward, {phase: CUDA event}
         # recorded on the stream that runs the phase (phase_times())
         self.phase_events = None
+        self._errors = L.DeviceErrorWatch()
 
     def _mark(self, name: str, stream) -> None:
         if self.phase_events is not None:
@@ -354,22 +355,31 @@ class DistributedDccKvLayer:
         exp_kv = (self.n_local, self.hkv, self.L, self.d)
         if tuple(q.shape) != exp_q or tuple(k.shape) != exp_kv or tuple(v.shape) != exp_kv:
             raise ValueError(f"expected local q {exp_q}, k/v {exp_kv}")
+        self._errors.poll()
         host = not q.is_cuda
         for t in (q, k, v):
             if t.dtype != self.dtype or not t.is_contiguous() or (not host and t.device != self.device) or \
                     (host and t.is_cuda):
                 raise ValueError(f"inputs must be contiguous {self.dtype}, all on {self.device} or all on the host")
         if host:
-            return self._forward_host(q, k, v, out)
+            out = self._forward_host(q, k, v, out)
+            self._errors.record(self._host_stream)
+            return out
         if self._host_stream is not None and self._last_call_host:
             # the internal buffers were last used by the host-buffer path's stream
             torch.cuda.current_stream(self.device).wait_stream(self._host_stream)
         self._last_call_host = False
         self._bind(q, k, v)
         self._run()
+        self._errors.record(torch.cuda.current_stream(self.device))
         return self.o_loc
 
     __call__ = forward
+
+    def check(self) -> None:
+        """Synchronise the device and raise ``DccError(DCC_ERR_TIMEOUT)`` if a
+        bounded device wait of any forward so far gave up on this rank."""
+        self._errors.check(self.device)
 
     def _peer(self, group_rank: int) -> int:
         return group_rank if self.group is None else dist.get_global_rank(self.group, group_rank)
@@ -568,8 +578,9 @@ class DistributedDccKvLayer:
     def launches_per_forward(self) -> int:
         sets = len(self.sets)
         pool = 0 if sets == 0 else 2 * -(-sets // 64)
+        # the last launch reports the bounded-wait error flags to the host
         return (pool + build_launch_count(len(self.build), self.code, self.d) + -(-len(self.local_problems) // 8)
-                + -(-len(self.compact_problems) // 8) + -(-len(self.helper_problems) // 8) + len(self.merges))
+                + -(-len(self.compact_problems) // 8) + -(-len(self.helper_problems) // 8) + len(self.merges) + 1)
 
 
 class DistributedDccKvStack:
@@ -596,6 +607,7 @@ class DistributedDccKvStack:
         (internal buffers, reused by the next call); complete once the
         current stream is synchronized."""
         first = self.slots[0]
+        first._errors.poll()
         dev = first.device
         main = torch.cuda.current_stream(dev)
         exp_q = (first.n_local, first.hq, first.L, first.d)
@@ -620,6 +632,7 @@ class DistributedDccKvStack:
             done = torch.cuda.Event()
             slot._run(side_waits=waits, done=done)
             self._done[li % 2] = done
+        first._errors.record(main)
         return self._outs[:len(inputs)]
 
     __call__ = forward

@@ -103,6 +103,7 @@ class DccKvSyncLayer:
         # each attention launch
         self.timing_events = None
         self.timing_index = 0
+        self._errors = L.DeviceErrorWatch()
 
     # -- descriptors (rebuilt only when the input tensors change) ------------
     def _bind(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: Optional[torch.Tensor] = None) -> None:
@@ -201,8 +202,11 @@ class DccKvSyncLayer:
         call streams them in block by block and returns ``out`` (or an
         internal pinned host buffer); like a ``non_blocking`` copy it is
         complete once the current stream is synchronized."""
+        self._errors.poll()
         if not q.is_cuda:
-            return self._forward_host(q, k, v, out)
+            out = self._forward_host(q, k, v, out)
+            self._errors.record(self._host_stream)
+            return out
         self.check_inputs(q, k, v)
         if self._host_stream is not None and self._last_call_host:
             # the internal buffers were last used by the host-buffer path's stream
@@ -214,9 +218,16 @@ class DccKvSyncLayer:
         else:
             self._ensure_streams()
             self._run_blocks(pool_all=True)
+        self._errors.record(torch.cuda.current_stream(self.device))
         return self.out
 
     __call__ = forward
+
+    def check(self) -> None:
+        """Synchronise the device and raise ``DccError(DCC_ERR_TIMEOUT)`` if a
+        bounded device wait of any forward so far gave up (each forward
+        checks the ones before it without synchronising)."""
+        self._errors.check(self.device)
 
     def _attention(self, problems) -> None:
         dev = self.device
@@ -390,7 +401,7 @@ class DccKvSyncLayer:
         else:
             build = sum(build_launch_count(len(self.build[part]), self.code, self.d) for part in self.build_of)
             attn = len(self.attn_problems)
-        return pool + build + attn
+        return pool + build + attn + 1  # + the error-flag report
 
     def compact(self, s: int, r: int, h: int):
         """The CompactKV C_{s->r} of KV head h from the last forward."""

@@ -246,6 +246,19 @@ int dcc_attention_fwd(const dcc_attn_problem* problems, int n_problems, int n_q_
 int dcc_device_error_status(int clear);
 /* The same for the tcgen05 scoring passes of the compact-KV build. */
 int dcc_build_error_status(int clear);
+/* Enqueues on `stream` one tiny kernel that writes the two bounded-wait
+ * error words (host_flags[0]: tcgen05 attention, host_flags[1]: tcgen05
+ * scoring) into caller-owned pinned host memory, device-accessible under
+ * unified addressing (no copy engine, no synchronisation).  Non-zero once
+ * the stream has passed the kernel means a wait expired; the
+ * layers read the pair at their next call instead of synchronising.  No
+ * counterpart in the reference, whose CPU path has no device waits; the
+ * timeout maps to the RuntimeError style of comm.py:97-99. */
+int dcc_device_error_flags_async(unsigned int* host_flags, void* stream);
+/* Test hook for the error path: one warp waits `limit_ns` (at most 100 ms)
+ * on an mbarrier that nothing arrives at, then records a timeout in the
+ * attention error word -- a wait that runs out without any fault. */
+int dcc_debug_expire_wait(uint64_t limit_ns, void* stream);
 
 /* ---- online softmax ------------------------------------------------------
  * online_softmax_from_attention (online_softmax.py:52-89), batched: logits

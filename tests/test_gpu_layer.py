@@ -171,3 +171,33 @@ def test_layer_1m_variable_budgets_all_blocks_sampled():
     for r in range(nb):
         got = np64(out[r, g * group:(g + 1) * group][:, rows[r]])
         assert rel_err(got, ref[r]) < 2e-2, r
+
+
+def test_device_timeout_reaches_the_caller():
+    """A bounded device wait that runs out -- an mbarrier nothing arrives at,
+    10 ms limit, no fault -- surfaces as DccError(DCC_ERR_TIMEOUT): from the
+    layer's next call (each forward reports the error flags to pinned host
+    memory without synchronising) and from check().  The context stays
+    usable and the next forward is right again."""
+    from dcc_kv_b200 import _lib as L
+    from dcc_kv_b200.workloads import layer_inputs
+    nb, Lb, hq, hkv, d = 3, 256, 4, 2, 128
+    q, k, v = (t.to(dev()) for t in layer_inputs(nb, Lb, hq, hkv, d, device="cpu", first_seed=5))
+    layer = dk.DccKvSyncLayer(nb, Lb, hq, hkv, d, 64, window=64)
+    want = layer(q, k, v).clone()
+    layer.check()
+    stream = L.stream_ptr(dev())
+    L.check(L.lib().dcc_debug_expire_wait(10_000_000, stream), "debug_expire_wait")
+    layer(q, k, v)  # its flag report runs after the expired wait
+    torch.cuda.synchronize()
+    with pytest.raises(L.DccError) as err:
+        layer(q, k, v)
+    assert err.value.status == L.DCC_ERR_TIMEOUT
+    assert torch.equal(layer(q, k, v), want)
+    layer.check()
+    L.check(L.lib().dcc_debug_expire_wait(10_000_000, stream), "debug_expire_wait")
+    with pytest.raises(L.DccError) as err:
+        layer.check()
+    assert err.value.status == L.DCC_ERR_TIMEOUT
+    assert torch.equal(layer(q, k, v), want)
+    layer.check()
