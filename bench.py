@@ -742,7 +742,7 @@ def run_build(args):
             "e2e": {"value": ws / (e2e_ms * 1e-3), "unit": "edge builds/s", "h2d_bytes_per_step": int(h2d),
                     "d2h_bytes_per_step": int(d2h)},
             "gpu_launches": launches,
-            "roofline": {"kernel": "the whole build step (pooling, two tcgen05 scoring passes, top-k, six FP64 "
+            "roofline": {"kernel": "the whole build step (pooling, two tcgen05 scoring passes, top-k, three FP64 "
                                    "calibration launches) against HBM: latency-bound, see profiles/",
                          "bound": "hbm", "achieved": per_gpu, "peak": hbm, "unit": "GB/s", "frac": per_gpu / hbm,
                          "peak_source": f"{src} HBM copy", "traffic": None,

@@ -106,12 +106,12 @@ def build_problem(keys: torch.Tensor, values: torch.Tensor, repr_q: torch.Tensor
 
 def build_launch_count(n_problems: int, dtype_code: int, head_dim: int) -> int:
     """Kernel launches of one batched build (C-library batch caps: 128 edges per
-    flush; tcgen05 scoring 56 edges per launch; 6 calibration launches)."""
+    flush; tcgen05 scoring 56 edges per launch; 3 calibration launches)."""
     n, total = n_problems, 0
     while n > 0:
         k = min(n, 128)
         scoring = 2 * -(-k // 56) if (dtype_code == L.DCC_BF16 and head_dim == 128) else 2
-        total += scoring + 1 + 6
+        total += scoring + 1 + 3
         n -= k
     return total
 

@@ -44,7 +44,6 @@ static void carve(Workspace& ws, const dcc_build_problem& q, int dv, BuildDesc<A
   d.n_btiles = (int)((Bp + 63) / 64);
   const size_t parts = q.num_repr < Bp ? (size_t)d.n_btiles * 64 * 64 : 0;
   d.gpart = ws.take<double>(parts);
-  d.xpart = ws.take<double>(parts);
   d.W = ws.take<double>((size_t)64 * dv);
 }
 

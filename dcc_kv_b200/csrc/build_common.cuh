@@ -36,7 +36,6 @@ struct BuildDesc {
   double* Y;     // [M, dv]
   double* wv;    // [B'] NNLS weights, then beta
   double* gpart; // [n_btiles, 64, 64] partial Gram G G^T per 64-key tile (M < B')
-  double* xpart; // [n_btiles, 64, 64] partial Gram X X^T
   double* W;     // [64, dv] (X X^T + lam I)^-1 Y
   int32_t n_btiles;
   int32_t pad2;

@@ -10,14 +10,15 @@
 // values (value_regression.py:38-78): X = softmax(Q^ C_K^T * scale + beta / M),
 //   M < B' : C_V = X^T (X X^T + lam I)^-1 Y ;  B' <= M : (X^T X + lam I)^-1 X^T Y.
 //
-// Six launches; the GEMM-shaped parts run as grids over (64-key tile, problem):
+// Three launches: the two wide GEMM-shaped ends run as grids over (64-key
+// tile, problem); everything between them is one CTA per problem, so the
+// latency-bound middle of the chain costs one launch instead of four:
 //   calib_logits  logits, G and partial Grams G_t G_t^T per tile   [tiles x problems]
-//   calib_beta    sum of partial Grams, Cholesky, w, beta           [problems]
-//   calib_x       X = row softmax of (logits + beta / M)            [problems]
-//   calib_xgram   partial Grams X_t X_t^T                           [tiles x problems]
-//   calib_w       Y from the scoring partials, Cholesky, W          [problems]
+//   calib_solve   sum of partial Grams, Cholesky, w, beta; X = row softmax of
+//                 (logits + beta / M); X X^T over all tiles; Y from the
+//                 scoring partials, Cholesky, W                     [problems]
 //   calib_cv      C_V = X^T W per tile                              [tiles x problems]
-// Partial Grams are summed in tile order, so results do not depend on timing.
+// Every sum runs in a fixed order, so results do not depend on timing.
 #include "dense_fp64.cuh"
 
 namespace dcc {
@@ -139,20 +140,22 @@ __global__ void __launch_bounds__(256) calib_logits_kernel(const __grid_constant
   tile_gram(gs, p.gpart + (int64_t)tile * 4096);
 }
 
-// ---- 2. beta ---------------------------------------------------------------------------
+// ---- 2. beta (one CTA per problem; shared scratch from calib_solve) ---------------------
+struct SolveSmem {
+  double* gram;    // [64][kLdG]
+  double* gsm;     // [64][kLdG]  G / X (B' <= M), X tiles (M < B')
+  double* tv;      // [64] block mass
+  double* vv;      // [64]
+  double* res;     // [64]
+  double* diag;    // [64]
+  double* colbuf;  // [128]
+  double* ws;      // [64][dv + 1]
+};
+
 template <typename TIn, typename Acc>
-__global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__ BuildBatch<Acc> b,
-                                                         const BuildParams prm) {
-  const BuildDesc<Acc>& p = b.p[blockIdx.x];
+__device__ __forceinline__ void beta_stage(const BuildDesc<Acc>& p, const BuildParams& prm, const SolveSmem& sm) {
   const int Bp = cal_bp(p), M = p.M;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  double* gram = reinterpret_cast<double*>(smem_raw);  // [64][65]
-  double* gsm = gram + 64 * kLdG;                      // [64][65]
-  double* tv = gsm + 64 * kLdG;                        // [64]
-  double* vv = tv + 64;                                // [64]
-  double* res = vv + 64;                               // [64]
-  double* diag = res + 64;                             // [64]
-  double* colbuf = diag + 64;                          // [128]
+  double *gram = sm.gram, *gsm = sm.gsm, *tv = sm.tv, *vv = sm.vv, *res = sm.res;
   // block mass: given, or the pass-2 chunk sums in chunk order
   for (int a = threadIdx.x; a < 64; a += blockDim.x) {
     double s = 0.0;
@@ -167,6 +170,7 @@ __global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__
   }
   if (!(p.stages & kStageBeta)) {
     for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) p.wv[bb] = load_side<TIn>(p.in_beta, bb);
+    __syncthreads();
     return;
   }
   __syncthreads();
@@ -178,10 +182,10 @@ __global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__
       gram[a * kLdG + a2] = s + (a == a2 ? lb : 0.0);
     }
     __syncthreads();
-    chol64(gram, kLdG, M, diag, colbuf);
+    chol64(gram, kLdG, M, sm.diag, sm.colbuf);
     if (threadIdx.x < 64) vv[threadIdx.x] = tv[threadIdx.x];  // zero past M
     __syncthreads();
-    if (threadIdx.x < 32) chol64_solve_vec(gram, kLdG, diag, M, vv);
+    if (threadIdx.x < 32) chol64_solve_vec(gram, kLdG, sm.diag, M, vv);
     __syncthreads();
     for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) {
       double w = 0.0;
@@ -206,8 +210,8 @@ __global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__
       vv[bb] = s;
     }
     __syncthreads();
-    chol64(gram, kLdG, Bp, diag, colbuf);
-    if (threadIdx.x < 32) chol64_solve_vec(gram, kLdG, diag, Bp, vv);
+    chol64(gram, kLdG, Bp, sm.diag, sm.colbuf);
+    if (threadIdx.x < 32) chol64_solve_vec(gram, kLdG, sm.diag, Bp, vv);
     __syncthreads();
     if (threadIdx.x < Bp) vv[threadIdx.x] = fmax(vv[threadIdx.x], 0.0);
     __syncthreads();
@@ -237,17 +241,15 @@ __global__ void __launch_bounds__(256) calib_beta_kernel(const __grid_constant__
     else
       static_cast<float*>(p.out_bias)[bb] = (float)beta;
   }
+  __syncthreads();
 }
 
-// ---- 3. X = softmax_b(logits + beta / M), one warp per row, 8 rows per CTA --------------
+// ---- 3. X = softmax_b(logits + beta / M), one warp per row ------------------------------
 template <typename Acc>
-__global__ void __launch_bounds__(256) calib_x_kernel(const __grid_constant__ BuildBatch<Acc> b) {
-  const BuildDesc<Acc>& p = b.p[blockIdx.y];
-  if (!(p.stages & kStageValues)) return;
+__device__ __forceinline__ void x_stage(const BuildDesc<Acc>& p) {
   const int Bp = cal_bp(p), M = p.M;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int a = blockIdx.x * 8 + warp;
-  if (a < M) {
+  for (int a = warp; a < M; a += blockDim.x >> 5) {
     double* xr = p.X + (int64_t)a * Bp;
     double mx = -INFINITY;
     for (int bb = lane; bb < Bp; bb += 32) {
@@ -265,39 +267,58 @@ __global__ void __launch_bounds__(256) calib_x_kernel(const __grid_constant__ Bu
     sum = warp_sum(sum);
     for (int bb = lane; bb < Bp; bb += 32) xr[bb] = xr[bb] / sum;
   }
+  __syncthreads();
 }
 
-// ---- 4. partial Grams of X ---------------------------------------------------------------
+// ---- 4. X X^T + lam I over all 64-key tiles (M < B'), accumulated in tile order ---------
 template <typename Acc>
-__global__ void __launch_bounds__(256) calib_xgram_kernel(const __grid_constant__ BuildBatch<Acc> b) {
-  const BuildDesc<Acc>& p = b.p[blockIdx.y];
+__device__ __forceinline__ void xgram_stage(const BuildDesc<Acc>& p, double lam, const SolveSmem& sm) {
   const int Bp = cal_bp(p), M = p.M;
-  const int tile = blockIdx.x;
-  if (!(p.stages & kStageValues) || M >= Bp || tile >= p.n_btiles) return;
-  __shared__ double xs[64 * kLdG];
-  const int b0 = tile * kCalTile;
-  for (int e = threadIdx.x; e < 64 * kCalTile; e += blockDim.x) {
-    const int a = e / kCalTile, bb = e % kCalTile;
-    xs[a * kLdG + bb] = (a < M && b0 + bb < Bp) ? p.X[(int64_t)a * Bp + b0 + bb] : 0.0;
+  const int ta = threadIdx.x & 15, tb = threadIdx.x >> 4;
+  double acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+  double* xs = sm.gsm;
+  for (int b0 = 0; b0 < Bp; b0 += kCalTile) {
+    for (int e = threadIdx.x; e < 64 * kCalTile; e += blockDim.x) {
+      const int a = e / kCalTile, bb = e % kCalTile;
+      xs[a * kLdG + bb] = (a < M && b0 + bb < Bp) ? p.X[(int64_t)a * Bp + b0 + bb] : 0.0;
+    }
+    __syncthreads();
+#pragma unroll 4
+    for (int c = 0; c < kCalTile; ++c) {
+      double xa[4], xb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        xa[i] = xs[(ta + 16 * i) * kLdG + c];
+        xb[i] = xs[(tb + 16 * i) * kLdG + c];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fma(xa[i], xb[j], acc[i][j]);
+    }
+    __syncthreads();
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int a = ta + 16 * i, a2 = tb + 16 * j;
+      if (a < M && a2 < M) sm.gram[a * kLdG + a2] = acc[i][j] + (a == a2 ? lam : 0.0);
+    }
   __syncthreads();
-  tile_gram(xs, p.xpart + (int64_t)tile * 4096);
 }
 
 // ---- 5. Y, then W = (X X^T + lam I)^-1 Y   (B' <= M: C_V directly) ----------------------
+// For M < B' the Gram (with lam) is already in sm.gram.
 template <typename TIn, typename Acc>
-__global__ void __launch_bounds__(256) calib_w_kernel(const __grid_constant__ BuildBatch<Acc> b,
-                                                      const BuildParams prm) {
-  const BuildDesc<Acc>& p = b.p[blockIdx.x];
-  if (!(p.stages & kStageValues)) return;
+__device__ __forceinline__ void w_stage(const BuildDesc<Acc>& p, const BuildParams& prm, const SolveSmem& sm) {
   const int Bp = cal_bp(p), M = p.M, dv = prm.dv;
-  extern __shared__ __align__(16) unsigned char smem_raw[];
-  double* gram = reinterpret_cast<double*>(smem_raw);  // [64][65]
-  double* gsm = gram + 64 * kLdG;                      // [64][65]
-  double* ws = gsm + 64 * kLdG;                        // [64][dv+1]
+  double *gram = sm.gram, *gsm = sm.gsm, *ws = sm.ws;
   const int ldw = dv + 1;
-  double* diag = ws + 64 * ldw;                        // [64]
-  double* colbuf = diag + 64;                          // [128]
   for (int e = threadIdx.x; e < M * dv; e += blockDim.x) {  // Y, chunk order
     const double s = ordered_sum(p.yp + e, (int64_t)M * dv, p.n_chunks);
     p.Y[e] = s;
@@ -306,13 +327,7 @@ __global__ void __launch_bounds__(256) calib_w_kernel(const __grid_constant__ Bu
   const double lv = prm.lambda_value;
   // system size: M x M (push-through form) or B' x B' (literal form)
   const int n = M < Bp ? M : Bp;
-  if (M < Bp) {
-    for (int e = threadIdx.x; e < M * M; e += blockDim.x) {
-      const int a = e / M, a2 = e % M;
-      const double s = ordered_sum(p.xpart + a * 64 + a2, 4096, p.n_btiles);
-      gram[a * kLdG + a2] = s + (a == a2 ? lv : 0.0);
-    }
-  } else {
+  if (M >= Bp) {
     __syncthreads();
     for (int e = threadIdx.x; e < M * Bp; e += blockDim.x) gsm[(e / Bp) * kLdG + e % Bp] = p.X[e];
     __syncthreads();
@@ -327,14 +342,36 @@ __global__ void __launch_bounds__(256) calib_w_kernel(const __grid_constant__ Bu
     }
   }
   __syncthreads();
-  chol64(gram, kLdG, n, diag, colbuf);
-  chol64_solve(gram, kLdG, diag, n, ws, ldw, dv);
+  chol64(gram, kLdG, n, sm.diag, sm.colbuf);
+  chol64_solve(gram, kLdG, sm.diag, n, ws, ldw, dv);
   if (M < Bp) {
     for (int e = threadIdx.x; e < M * dv; e += blockDim.x) p.W[e] = ws[(e / dv) * ldw + e % dv];
   } else {
     TIn* outv = static_cast<TIn*>(p.out_values);
     for (int e = threadIdx.x; e < Bp * dv; e += blockDim.x) outv[e] = from_f64<TIn>(ws[(e / dv) * ldw + e % dv]);
   }
+}
+
+// stages 2-5, one CTA per problem
+template <typename TIn, typename Acc>
+__global__ void __launch_bounds__(256) calib_solve_kernel(const __grid_constant__ BuildBatch<Acc> b,
+                                                          const BuildParams prm) {
+  const BuildDesc<Acc>& p = b.p[blockIdx.x];
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  SolveSmem sm;
+  sm.gram = reinterpret_cast<double*>(smem_raw);
+  sm.gsm = sm.gram + 64 * kLdG;
+  sm.tv = sm.gsm + 64 * kLdG;
+  sm.vv = sm.tv + 64;
+  sm.res = sm.vv + 64;
+  sm.diag = sm.res + 64;
+  sm.colbuf = sm.diag + 64;
+  sm.ws = sm.colbuf + 128;
+  beta_stage<TIn, Acc>(p, prm, sm);
+  if (!(p.stages & kStageValues)) return;
+  x_stage(p);
+  if (p.M < cal_bp(p)) xgram_stage(p, prm.lambda_value, sm);
+  w_stage<TIn, Acc>(p, prm, sm);
 }
 
 // ---- 6. C_V = X^T W per 64-key tile --------------------------------------------------------
@@ -400,28 +437,19 @@ int launch_calibrate(const BuildBatch<Acc>& b, const BuildParams& prm, cudaStrea
   int tmax = 1;
   for (int i = 0; i < b.n; ++i) tmax = b.p[i].n_btiles > tmax ? b.p[i].n_btiles : tmax;
   const size_t smem1 = 3 * 64 * kLdG * sizeof(double);
-  const size_t smem5 = (2 * 64 * kLdG + 64 * (size_t)(prm.dv + 1) + 3 * 64) * sizeof(double);
+  const size_t smem2 = (2 * 64 * kLdG + 4 * 64 + 128 + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
   const size_t smem6 = (64 * kLdG + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
-  const size_t smem2 = (2 * 64 * kLdG + 6 * 64) * sizeof(double);
   auto k1 = calib_logits_kernel<TIn, Acc>;
-  auto k2 = calib_beta_kernel<TIn, Acc>;
-  auto k5 = calib_w_kernel<TIn, Acc>;
+  auto k2 = calib_solve_kernel<TIn, Acc>;
   auto k6 = calib_cv_kernel<TIn, Acc>;
   DCC_CHECK(check_cuda(cudaFuncSetAttribute(k1, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem1), "calib smem"));
   DCC_CHECK(check_cuda(cudaFuncSetAttribute(k2, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem2), "calib smem"));
-  DCC_CHECK(check_cuda(cudaFuncSetAttribute(k5, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem5), "calib smem"));
   DCC_CHECK(check_cuda(cudaFuncSetAttribute(k6, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem6), "calib smem"));
   const dim3 tiles(tmax, b.n);
   k1<<<tiles, 256, smem1, st>>>(b, prm);
   DCC_CHECK(check_launch("calib_logits"));
   k2<<<b.n, 256, smem2, st>>>(b, prm);
-  DCC_CHECK(check_launch("calib_beta"));
-  calib_x_kernel<Acc><<<dim3(kMaxRepr / 8, b.n), 256, 0, st>>>(b);
-  DCC_CHECK(check_launch("calib_x"));
-  calib_xgram_kernel<Acc><<<tiles, 256, 0, st>>>(b);
-  DCC_CHECK(check_launch("calib_xgram"));
-  k5<<<b.n, 256, smem5, st>>>(b, prm);
-  DCC_CHECK(check_launch("calib_w"));
+  DCC_CHECK(check_launch("calib_solve"));
   k6<<<tiles, 256, smem6, st>>>(b, prm);
   return check_launch("calib_cv");
 }

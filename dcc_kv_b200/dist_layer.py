@@ -22,11 +22,12 @@ blocks; round-robin would give 4 to 10).  One forward on every rank:
      read in place from the receive / local buffers, continuing each
      block's online softmax from the local (O, LSE) in place -- the merge
      (online_softmax.py:92-111) happens inside that launch;
-  5. with one block per rank only (``default_help``): a heavy block's first
-     sources are consumed on its mirror block's rank -- its queries go there
-     once (point-to-point on a communicator of their own, so the transfer
-     waits only for the inputs), that rank runs them over the handed
-     sources, and the partial (O, LSE) comes back and is merged.
+  5. with one block per rank only (``default_help``): the compact attention
+     of a heavy block's first KV heads runs on its mirror block's rank -- the
+     query heads of those KV heads go there once (point-to-point on a
+     communicator of their own, so the transfer waits only for the inputs),
+     the builds route those KV heads of every source edge there, that rank
+     attends with them, and the partial (O, LSE) comes back and is merged.
 
 ``DistPlan`` is the pure host-side routing (offsets and split sizes),
 identical on every rank and testable without a GPU.
@@ -60,44 +61,96 @@ def local_blocks_of(n_blocks: int, world: int, rank: int) -> List[int]:
     return [b for b in range(n_blocks) if block_owner(b, world) == rank]
 
 
-def default_help(n_blocks: int, world: int) -> Dict[int, int]:
+# Cost model of the hand-off, in FLOP-equivalents of attention work (measured
+# on B200 with the 128K layer at one block per GPU): a build problem (one
+# edge and KV head) slows the attention it shares the GPU with by ~7.9e9
+# FLOP-equivalents per 16384 source keys; a byte handed to or from the
+# helper costs ~3.7e3 (NCCL point-to-point ~270 GB/s against ~1e15 FLOP/s
+# of attention).
+BUILD_FLOP_PER_16K_KEYS = 7.9e9
+HANDOFF_FLOP_PER_BYTE = 3.7e3
+
+
+def default_help(n_blocks: int, world: int, block_len: int, n_kv_heads: int, q_per_kv: int, head_dim: int,
+                 budgets, elem_bytes: int = 2) -> Dict[int, int]:
     """With one block per rank the compact attention is unbalanced (block r
-    attends to r compact blocks): block r > its mirror p = n_blocks - 1 - r
-    hands its first (r - p) // 2 sources to p's rank, which computes that
-    part of r's compact attention.  Returns {r: number of helped sources}."""
+    attends to r compact blocks, and block s builds n_blocks - 1 - s edges).
+    Block r > its mirror p = n_blocks - 1 - r hands the compact attention of
+    its first k KV heads (their q_per_kv query heads each) to p's rank; k
+    minimises the larger of the two ranks' estimated work (local causal
+    attention + builds + compact attention + the return of the helper's
+    partial output; the query transfer runs under the local attention).
+    Returns {r: k} for the hand-offs that save at least 2 %."""
     if world != n_blocks:
         return {}
+    table = budget_table(n_blocks, budgets)
+    L, hq = block_len, n_kv_heads * q_per_kv
+    pair = 4.0 * head_dim  # FLOPs per (query row, key) per query head
+    local = L * (L + 1) / 2 * hq * pair
+    build = BUILD_FLOP_PER_16K_KEYS * L / 16384.0
+
+    def compact(b):
+        return L * hq * pair * sum(min(table[(s, b)], L) for s in range(b))
+
+    def builds(b):
+        return (n_blocks - 1 - b) * n_kv_heads * build
+
     help_ = {}
     for r in range(n_blocks):
         p = n_blocks - 1 - r
-        if r > p and (r - p) // 2 > 0:
-            help_[r] = (r - p) // 2
+        if r <= p:
+            continue
+        best_k, best_t = 0, None
+        for k in range(n_kv_heads):
+            f = k / n_kv_heads
+            # the partial output comes back after the helper's attention; the
+            # query transfer runs under the local attention and is not counted
+            xfer = k * q_per_kv * L * head_dim * elem_bytes * HANDOFF_FLOP_PER_BYTE
+            t_owner = local + builds(r) + (1 - f) * compact(r)
+            t_helper = local + builds(p) + compact(p) + f * compact(r) + xfer
+            t = max(t_owner, t_helper)
+            if best_t is None or t < best_t:
+                best_k, best_t = k, t
+        # a hand-off that saves under 2 % is not worth its transfers and merge
+        t_none = max(local + builds(r) + compact(r), local + builds(p) + compact(p))
+        if best_k > 0 and best_t < 0.98 * t_none:
+            help_[r] = best_k
     return help_
 
 
 class DistPlan:
-    """Routing of every compact-KV edge (s -> r, s < r) for G ranks.  An edge
-    goes to the rank that consumes it: the owner of r, or, for the first
-    ``help[r]`` sources of a helped block r, the owner of r's mirror block."""
+    """Routing of every compact-KV edge (s -> r, s < r) for G ranks, per KV
+    head: head g of edge (s, r) goes to the rank that attends with it -- the
+    owner of r, or, for the first ``help[r]`` KV heads of a helped block r,
+    the owner of r's mirror block.  Units (s, r, g) sit in a buffer in
+    (r, s, g) order, so the heads of one edge on one rank are contiguous."""
 
     def __init__(self, n_blocks: int, world: int, block_len: int, n_kv_heads: int, head_dim: int,
-                 budgets: Budgets, elem_bytes: int = 2, help_sources: Optional[Dict[int, int]] = None):
+                 budgets: Budgets, elem_bytes: int = 2, help_heads: Optional[Dict[int, int]] = None,
+                 q_per_kv: int = 4):
         if n_blocks % world:
             raise ValueError(f"{n_blocks} blocks do not split evenly over {world} ranks")
-        self.nb, self.world, self.L = n_blocks, world, block_len
+        self.nb, self.world, self.L, self.hkv = n_blocks, world, block_len, n_kv_heads
         self.n_local = n_blocks // world
         self.budgets = budget_table(n_blocks, budgets)
         self.layout = {e: EdgeLayout(n_kv_heads, min(b, block_len), head_dim, elem_bytes)
                        for e, b in self.budgets.items()}
-        self.help = dict(default_help(n_blocks, world) if help_sources is None else help_sources)
+        if help_heads is None:
+            help_heads = default_help(n_blocks, world, block_len, n_kv_heads, q_per_kv, head_dim,
+                                      self.budgets, elem_bytes)
+        self.help = {r: k for r, k in help_heads.items() if k > 0}
         for r, k in self.help.items():
-            if not (0 <= k <= r) or self.helper(r) == self.owner(r) or self.n_local != 1:
-                raise ValueError(f"block {r}: cannot hand {k} sources to rank {self.helper(r)}")
-        # bytes from rank i to rank j: edges (s on i, consumed on j), ordered by (r, s)
-        self.edges_ij = {(i, j): sorted(((s, r) for (s, r) in self.budgets if self.owner(s) == i
-                                         and self.consumer((s, r)) == j), key=lambda e: (e[1], e[0]))
-                         for i in range(world) for j in range(world)}
-        self.bytes_ij = {ij: sum(self.layout[e].nbytes for e in es) for ij, es in self.edges_ij.items()}
+            if not (0 < k < n_kv_heads) or not (0 < r < n_blocks) or self.helper(r) == self.owner(r) \
+                    or self.n_local != 1:
+                raise ValueError(f"block {r}: cannot hand {k} KV heads to rank {self.helper(r)}")
+        units = sorted(((s, r, g) for (s, r) in self.budgets for g in range(n_kv_heads)),
+                       key=lambda u: (u[1], u[0], u[2]))
+        # units from rank i to rank j, in (r, s, g) order
+        self.units_ij = {(i, j): [] for i in range(world) for j in range(world)}
+        for u in units:
+            self.units_ij[(self.owner(u[0]), self.consumer(u))].append(u)
+        self.bytes_ij = {ij: sum(self.layout[(u[0], u[1])].head_bytes for u in us)
+                         for ij, us in self.units_ij.items()}
 
     def owner(self, b: int) -> int:
         return block_owner(b, self.world)
@@ -106,14 +159,24 @@ class DistPlan:
         """Rank that takes part of block r's compact attention (its mirror's owner)."""
         return self.owner(self.nb - 1 - r)
 
-    def consumer(self, e: Tuple[int, int]) -> int:
-        """Rank whose attention reads edge e = (s, r)."""
+    def consumer(self, u: Tuple[int, ...]) -> int:
+        """Rank whose attention reads KV head g of edge (s, r), u = (s, r, g)."""
+        s, r, g = u
+        return self.helper(r) if g < self.help.get(r, 0) else self.owner(r)
+
+    def heads_on(self, rank: int, e: Tuple[int, int]) -> Tuple[int, int]:
+        """KV heads [lo, hi) of edge e that ``rank`` attends with (lo == hi: none)."""
         s, r = e
-        return self.helper(r) if s < self.help.get(r, 0) else self.owner(r)
+        k = self.help.get(r, 0)
+        if rank == self.owner(r):
+            return (k, self.hkv)
+        if k > 0 and rank == self.helper(r):
+            return (0, k)
+        return (0, 0)
 
     def helped_by(self, rank: int) -> List[int]:
         """Blocks of other ranks part of whose compact attention ``rank`` computes."""
-        return [r for r, k in sorted(self.help.items()) if k > 0 and self.helper(r) == rank]
+        return [r for r in sorted(self.help) if self.helper(r) == rank]
 
     def local_index(self, b: int) -> int:
         return self.local_blocks(self.owner(b)).index(b)
@@ -127,33 +190,28 @@ class DistPlan:
     def recv_splits(self, rank: int) -> List[int]:
         return [0 if i == rank else self.bytes_ij[(i, rank)] for i in range(self.world)]
 
-    def send_offsets(self, rank: int) -> Dict[Tuple[int, int], Tuple[str, int]]:
-        """Where rank's builds write each outgoing edge: ("send"|"local", byte offset)."""
+    def _place(self, units, buf, out, off=0):
+        for u in units:
+            out[u] = (buf, off)
+            off += self.layout[(u[0], u[1])].head_bytes
+        return off
+
+    def send_offsets(self, rank: int) -> Dict[Tuple[int, int, int], Tuple[str, int]]:
+        """Where rank's builds write each outgoing unit (s, r, g): ("send"|"local", byte offset)."""
         out, off = {}, 0
         for j in range(self.world):
-            if j == rank:
-                continue
-            for e in self.edges_ij[(rank, j)]:
-                out[e] = ("send", off)
-                off += self.layout[e].nbytes
-        off = 0
-        for e in self.edges_ij[(rank, rank)]:
-            out[e] = ("local", off)
-            off += self.layout[e].nbytes
+            if j != rank:
+                off = self._place(self.units_ij[(rank, j)], "send", out, off)
+        self._place(self.units_ij[(rank, rank)], "local", out)
         return out
 
-    def recv_offsets(self, rank: int) -> Dict[Tuple[int, int], Tuple[str, int]]:
-        """Where each edge that rank consumes sits: ("recv"|"local", byte offset)."""
+    def recv_offsets(self, rank: int) -> Dict[Tuple[int, int, int], Tuple[str, int]]:
+        """Where each unit that rank attends with sits: ("recv"|"local", byte offset)."""
         out, off = {}, 0
         for i in range(self.world):
-            if i == rank:
-                continue
-            for e in self.edges_ij[(i, rank)]:
-                out[e] = ("recv", off)
-                off += self.layout[e].nbytes
-        for e, loc in self.send_offsets(rank).items():
-            if loc[0] == "local":
-                out[e] = loc
+            if i != rank:
+                off = self._place(self.units_ij[(i, rank)], "recv", out, off)
+        self._place(self.units_ij[(rank, rank)], "local", out)
         return out
 
 
@@ -166,17 +224,20 @@ class DistributedDccKvLayer:
                  budgets: Budgets, window: int, num_representative_queries: int = 64, projection_dim: int = 32,
                  lambda_beta: float = 1e-3, lambda_value: float = 1e-3, seed: int = 42,
                  dtype: torch.dtype = torch.bfloat16, device=None, group=None,
-                 help_sources: Optional[Dict[int, int]] = None, p2p_group=None):
-        """``help_sources`` ({block: sources}) overrides the default hand-off
+                 help_heads: Optional[Dict[int, int]] = None, p2p_group=None):
+        """``help_heads`` ({block: KV heads}) overrides the default hand-off
         of compact attention from heavy blocks to their mirror's rank (see
-        ``default_help``; only with one block per rank).  The hand-off's
-        point-to-point transfers run on ``p2p_group``, a communicator of
-        their own with the ranks of ``group``: NCCL runs the operations of
-        one communicator in issue order on one internal stream, so on the
-        exchange's communicator the query transfer would queue behind the
-        all-to-allv, which waits for the builds.  By default every rank of
-        the default group creates it here (a collective call); with a
-        sub-``group``, pass it, else the transfers share ``group``."""
+        ``default_help``; only with one block per rank).
+
+        Communicators: with ``group`` None every rank creates two of its own
+        here (collective calls), both with high-priority NCCL streams, so
+        their kernels are dispatched ahead of the attention that fills the
+        GPU: one for the exchange (all-gather and all-to-allv) and one for
+        the hand-off's point-to-point transfers.  NCCL runs the operations
+        of one communicator in issue order on one internal stream, so on a
+        shared one the query transfer would queue behind the all-to-allv,
+        which waits for the builds.  With a sub-``group`` the exchange runs
+        on it, and the transfers on ``p2p_group`` if given, else on it too."""
         self.group = group
         self.rank = dist.get_rank(group)
         self.world = dist.get_world_size(group)
@@ -190,7 +251,7 @@ class DistributedDccKvLayer:
         self.dtype = dtype
         self.code = L.dtype_code(torch.empty(0, dtype=dtype))
         self.plan = DistPlan(n_blocks, self.world, block_len, n_kv_heads, head_dim, budgets,
-                             torch.empty(0, dtype=dtype).element_size(), help_sources)
+                             torch.empty(0, dtype=dtype).element_size(), help_heads, self.qgroup)
         self.n_local = self.plan.n_local
         self.local_blocks = self.plan.local_blocks(self.rank)
         dev = self.device
@@ -208,30 +269,39 @@ class DistributedDccKvLayer:
         self.bufs = {"send": self.send_buf, "recv": self.recv_buf, "local": self.local_buf}
         # per-edge selected indices stay on the source rank
         self.sel_idx = {e: torch.empty(n_kv_heads, self.plan.layout[e].rows, dtype=torch.int64, device=dev)
-                        for e, loc in self.plan.send_offsets(self.rank).items()}
+                        for e in sorted({(s, r) for (s, r, g) in self.plan.send_offsets(self.rank)})}
         self.o_loc = torch.empty(self.n_local, n_q_heads, block_len, head_dim, dtype=dtype, device=dev)
         self.lse_loc = torch.empty(self.n_local, n_q_heads, block_len, dtype=torch.float32, device=dev)
         # compact attention handed between mirror ranks (one block per rank):
-        # a helped block's queries go to the helper, the helper's partial
-        # (O, LSE) over the handed sources comes back and is merged
-        self.helped = [r for r in self.local_blocks if self.plan.help.get(r, 0) > 0]
+        # the query heads of a helped block's first KV heads go to the
+        # helper, which attends with those heads of every compact source; its
+        # partial (O, LSE) for them comes back and is merged
+        self.helped = [r for r in self.local_blocks if r in self.plan.help]
         self.helping = self.plan.helped_by(self.rank)
-        qshape, lshape = (n_q_heads, block_len, head_dim), (n_q_heads, block_len)
-        self.q_help = {r: torch.empty(qshape, dtype=dtype, device=dev) for r in self.helping}
-        self.o_help = {r: torch.empty(qshape, dtype=dtype, device=dev) for r in self.helping}
-        self.lse_help = {r: torch.empty(lshape, dtype=torch.float32, device=dev) for r in self.helping}
-        self.o_from = {r: torch.empty(qshape, dtype=dtype, device=dev) for r in self.helped}
-        self.lse_from = {r: torch.empty(lshape, dtype=torch.float32, device=dev) for r in self.helped}
+        g = self.qgroup
+
+        def qshape(r):
+            return (self.plan.help[r] * g, block_len, head_dim)
+
+        self.q_help = {r: torch.empty(qshape(r), dtype=dtype, device=dev) for r in self.helping}
+        self.o_help = {r: torch.empty(qshape(r), dtype=dtype, device=dev) for r in self.helping}
+        self.lse_help = {r: torch.empty(qshape(r)[:2], dtype=torch.float32, device=dev) for r in self.helping}
+        self.o_from = {r: torch.empty(qshape(r), dtype=dtype, device=dev) for r in self.helped}
+        self.lse_from = {r: torch.empty(qshape(r)[:2], dtype=torch.float32, device=dev) for r in self.helped}
         self.p2p_stream = torch.cuda.Stream(device=dev)
-        self.p2p_group = p2p_group
-        if self.plan.help and p2p_group is None:
-            if group is None:
-                self.p2p_group = dist.new_group(ranks=list(range(self.world)))
+        self.xgroup, self.p2p_group = group, p2p_group
+        if group is None and self.world > 1 and dist.get_backend() == "nccl":
+            opts = dist.ProcessGroupNCCL.Options()
+            opts.is_high_priority_stream = True
+            ranks = list(range(self.world))
+            self.xgroup = dist.new_group(ranks=ranks, pg_options=opts)
+            if self.plan.help and p2p_group is None:
+                self.p2p_group = dist.new_group(ranks=ranks, pg_options=opts)
                 # the first operation on a communicator must involve all of
                 # its ranks; the hand-off transfers involve only some
                 dist.barrier(group=self.p2p_group)
-            else:
-                self.p2p_group = group
+        if self.p2p_group is None:
+            self.p2p_group = self.xgroup
         # pooling, the gather, the builds and the exchange run on a high-priority
         # side stream, so their kernels are dispatched ahead of the local
         # attention that fills the GPU meanwhile on the main stream
@@ -287,7 +357,7 @@ class DistributedDccKvLayer:
             if len(self._bindings) >= 8:
                 self._bindings.pop(next(iter(self._bindings)))
             self._bindings[key] = bound
-        (self.sets, self.build, self.local_problems, self.compact_problems, self.helper_problems, self.merges,
+        (self.sets, self.build, self.local_problems, self.compact_calls, self.helper_calls, self.merges,
          need) = bound
         if need > self._ws_bytes:
             # the workspace may still be in use by the side stream
@@ -302,14 +372,13 @@ class DistributedDccKvLayer:
                 for li, b in enumerate(self.local_blocks) if b > 0 for h in range(self.hkv)]
         send_off = self.plan.send_offsets(self.rank)
         build = []
-        for (s, r), (buf, off) in sorted(send_off.items()):
+        for (s, r, h), (buf, off) in sorted(send_off.items()):
             lay = self.plan.layout[(s, r)]
-            ko, vo, bo = lay.views(self.bufs[buf], off, self.dtype)
+            ko, vo, bo = lay.views(self.bufs[buf], off, self.dtype, n_heads=1)
             rep = self.repr_all[self.plan.owner(r), self.plan.local_index(r)]
             ls = self.plan.local_index(s)
-            for h in range(self.hkv):
-                build.append(build_problem(k[ls, h], v[ls, h], rep[h], self.plan.budgets[(s, r)], ko[h], vo[h],
-                                           bo[h], self.sel_idx[(s, r)][h], num_repr=self.m_eff))
+            build.append(build_problem(k[ls, h], v[ls, h], rep[h], self.plan.budgets[(s, r)], ko[0], vo[0],
+                                       bo[0], self.sel_idx[(s, r)][h], num_repr=self.m_eff))
         need = 0
         if build:
             arr = (L.dcc_build_problem * len(build))(*build)
@@ -317,33 +386,48 @@ class DistributedDccKvLayer:
         local_problems = [attn_problem(q[li], o[li], lse[li], [kv_segment(k[li], v[li])],
                                        causal=True) for li in range(self.n_local)]
         recv_off = self.plan.recv_offsets(self.rank)
-        # the compact blocks continue each local block's online softmax from
-        # its (O, LSE), in place: the merge needs no separate pass
-        compact_problems, merges = [], []
 
         def consumed_segments(r):
-            segs = []
+            """This rank's KV heads [lo, hi) of every compact source of block r."""
+            segs, heads = [], None
             for s in range(r):
-                if self.plan.consumer((s, r)) != self.rank:
+                lo, hi = self.plan.heads_on(self.rank, (s, r))
+                if lo == hi:
                     continue
-                buf, off = recv_off[(s, r)]
-                ko, vo, bo = self.plan.layout[(s, r)].views(self.bufs[buf], off, self.dtype)
+                heads = (lo, hi)
+                buf, off = recv_off[(s, r, lo)]
+                ko, vo, bo = self.plan.layout[(s, r)].views(self.bufs[buf], off, self.dtype, n_heads=hi - lo)
                 segs.append(kv_segment(ko, vo, bo))
-            return segs
+            return segs, heads
 
+        # the compact blocks continue each local block's online softmax from
+        # its (O, LSE), in place: the merge needs no separate pass.  Launches
+        # are grouped by head range: (problems, first query head, query heads).
+        compact_calls, merges = [], []
+        plain = []
         for li, r in enumerate(self.local_blocks):
-            segs = consumed_segments(r)
-            helped = r in self.helped
-            if segs:
-                # a helped block also needs the LSE of its own part for the final merge
-                compact_problems.append(attn_problem(q[li], o[li], lse[li] if helped else None, segs,
-                                                     o_init=o[li], lse_init=lse[li]))
-            if helped:
-                merges.append((q[li], o[li], lse[li], r))
-        # this rank's part of other ranks' blocks: their queries over the handed sources
-        helper_problems = [attn_problem(self.q_help[r], self.o_help[r], self.lse_help[r], consumed_segments(r))
-                           for r in self.helping]
-        return sets, build, local_problems, compact_problems, helper_problems, merges, need
+            segs, heads = consumed_segments(r)
+            if r in self.helped:
+                # this rank attends with KV heads [k, H_kv) (query heads [k g, H_q));
+                # the helper's partial for query heads [0, k g) is merged afterwards
+                kq = self.plan.help[r] * g
+                if segs:
+                    compact_calls.append(([attn_problem(q[li, kq:], o[li, kq:], None, segs,
+                                                        o_init=o[li, kq:], lse_init=lse[li, kq:])],
+                                          self.hq - kq, self.hkv - kq // g))
+                merges.append((q[li, :kq], o[li, :kq], lse[li, :kq], r))
+            elif segs:
+                plain.append(attn_problem(q[li], o[li], None, segs, o_init=o[li], lse_init=lse[li]))
+        if plain:
+            compact_calls.insert(0, (plain, self.hq, self.hkv))
+        # this rank's part of other ranks' blocks: their first query heads over
+        # those KV heads of every source
+        helper_calls = []
+        for r in self.helping:
+            segs, _ = consumed_segments(r)
+            kq = self.plan.help[r] * g
+            helper_calls.append(([attn_problem(self.q_help[r], self.o_help[r], self.lse_help[r], segs)], kq, kq // g))
+        return sets, build, local_problems, compact_calls, helper_calls, merges, need
 
     def forward(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor = None) -> torch.Tensor:
         """Local blocks q [n_local, H_q, L, d], k / v [n_local, H_kv, L, d] ->
@@ -425,7 +509,7 @@ class DistributedDccKvLayer:
                 side.wait_event(windows_ready)
             select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
             self._mark("pooling", side)
-            dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.group)
+            dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.xgroup)
             self._mark("gather", side)
             if kv_ready is not None:
                 side.wait_event(kv_ready)
@@ -433,7 +517,7 @@ class DistributedDccKvLayer:
             self._mark("builds", side)
             ns, nr = sum(self.send_splits), sum(self.recv_splits)
             dist.all_to_all_single(self.recv_buf[:nr], self.send_buf[:ns], output_split_sizes=self.recv_splits,
-                                   input_split_sizes=self.send_splits, group=self.group)
+                                   input_split_sizes=self.send_splits, group=self.xgroup)
             self._mark("exchange", side)
         # helped blocks' queries to their helpers (after the collectives in
         # issue order, on a stream that waits only for the inputs)
@@ -465,14 +549,16 @@ class DistributedDccKvLayer:
         self._mark("local_attention", main)
         main.wait_stream(side)
         self._mark("exchange_wait", main)
-        run_attention(self.compact_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code, dev)
+        scale = 1.0 / math.sqrt(self.d)
+        for probs, hq, hkv in self.compact_calls:
+            run_attention(probs, hq, hkv, self.d, scale, self.code, dev)
         self._mark("compact_attention", main)
         if self.helped or self.helping:
             for req in q_reqs:
                 req.wait()  # the main stream waits for the query transfers
             if self.helping:
-                run_attention(self.helper_problems, self.hq, self.hkv, self.d, 1.0 / math.sqrt(self.d), self.code,
-                              dev)
+                for probs, hq, hkv in self.helper_calls:
+                    run_attention(probs, hq, hkv, self.d, scale, self.code, dev)
                 self._mark("helper_attention", main)
             # partial states back to the helped blocks' ranks, merged there
             ops = []
@@ -580,7 +666,7 @@ class DistributedDccKvLayer:
         pool = 0 if sets == 0 else 2 * -(-sets // 64)
         # the last launch reports the bounded-wait error flags to the host
         return (pool + build_launch_count(len(self.build), self.code, self.d) + -(-len(self.local_problems) // 8)
-                + -(-len(self.compact_problems) // 8) + -(-len(self.helper_problems) // 8) + len(self.merges) + 1)
+                + sum(-(-len(c[0]) // 8) for c in self.compact_calls + self.helper_calls) + len(self.merges) + 1)
 
 
 class DistributedDccKvStack:

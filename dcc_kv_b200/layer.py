@@ -13,7 +13,7 @@ Layout (HBM): block-major, head-major, contiguous --
 All buffers and kernel descriptors are built once per shape; ``forward``
 on device inputs only enqueues kernels on the current stream:
     1 projection + 1 FPS launch       (all (destination, KV head) sets)
-    9 build launches per <=128 edges  (score stats, score probs, top-k, six
+    6 build launches per <=128 edges  (score stats, score probs, top-k, three
                                        calibration launches)
     1 attention launch: per block its causal local segment followed by its
       compact segment with the logit bias, one online softmax over both (the

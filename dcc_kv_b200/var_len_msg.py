@@ -3,15 +3,18 @@ CompactKV wire format used by the distributed layer.
 
 ``pack_var_len_messages`` / ``unpack_var_len_messages`` / ``mock_all_to_allv``
 keep the reference's signatures and assertions.  The wire format of one
-edge's compact KV (all KV heads) is a byte block
+edge's compact KV is KV-head-major: per KV head a byte block
 
-    keys   [H_kv, B', d]  (input dtype)
-    values [H_kv, B', d]  (input dtype)
-    bias   [H_kv, B']     float32
+    keys   [B', d]  (input dtype)
+    values [B', d]  (input dtype)
+    bias   [B']     float32
     padding to a multiple of 256 bytes
 
-so every keys / values / bias block starts 16-byte aligned (TMA operands)
-and a destination attends to it in place, one KV segment per edge.
+so every keys / values / bias block starts 16-byte aligned (TMA operands),
+a destination attends to it in place (one KV segment per edge, head stride
+= the block size), and any run of consecutive KV heads of an edge is one
+contiguous byte range -- an edge can be split by KV heads between two
+consuming ranks without a copy.
 """
 from __future__ import annotations
 
@@ -66,7 +69,7 @@ def _align(n: int, a: int = 256) -> int:
 
 @dataclass(frozen=True)
 class EdgeLayout:
-    """Byte layout of one edge's compact KV block."""
+    """Byte layout of one edge's compact KV block (KV-head-major)."""
     n_kv_heads: int
     rows: int        # B' = min(budget, L_s)
     head_dim: int
@@ -74,7 +77,8 @@ class EdgeLayout:
 
     @property
     def kv_bytes(self) -> int:
-        return self.n_kv_heads * self.rows * self.head_dim * self.elem
+        """Bytes of one head's keys (or values)."""
+        return self.rows * self.head_dim * self.elem
 
     @property
     def keys_off(self) -> int:
@@ -89,14 +93,26 @@ class EdgeLayout:
         return 2 * self.kv_bytes
 
     @property
-    def nbytes(self) -> int:
-        return _align(2 * self.kv_bytes + self.n_kv_heads * self.rows * 4)
+    def head_bytes(self) -> int:
+        return _align(2 * self.kv_bytes + self.rows * 4)
 
-    def views(self, buf: torch.Tensor, offset: int, dtype: torch.dtype):
-        """(keys [H, B', d], values [H, B', d], bias [H, B']) views of ``buf``
-        (uint8) at ``offset``."""
-        h, b, d = self.n_kv_heads, self.rows, self.head_dim
-        k = buf[offset + self.keys_off: offset + self.keys_off + self.kv_bytes].view(dtype).view(h, b, d)
-        v = buf[offset + self.values_off: offset + self.values_off + self.kv_bytes].view(dtype).view(h, b, d)
-        bias = buf[offset + self.bias_off: offset + self.bias_off + h * b * 4].view(torch.float32).view(h, b)
+    @property
+    def nbytes(self) -> int:
+        return self.n_kv_heads * self.head_bytes
+
+    def views(self, buf: torch.Tensor, offset: int, dtype: torch.dtype, n_heads: int = None):
+        """(keys [n, B', d], values [n, B', d], bias [n, B']) views of ``n``
+        consecutive head blocks (default: all heads) of ``buf`` (uint8, a
+        multiple of 256 bytes long) starting at byte ``offset``."""
+        n = self.n_kv_heads if n_heads is None else n_heads
+        b, d, hb = self.rows, self.head_dim, self.head_bytes
+        if offset % 256 or buf.numel() % 256 or offset + n * hb > buf.numel():
+            raise ValueError("edge views need 256-byte aligned offsets inside the buffer")
+        elem = torch.empty(0, dtype=dtype).element_size()
+        typed = buf.view(dtype)
+        base = typed.storage_offset() + offset // elem
+        k = typed.as_strided((n, b, d), (hb // elem, d, 1), base + self.keys_off // elem)
+        v = typed.as_strided((n, b, d), (hb // elem, d, 1), base + self.values_off // elem)
+        fl = buf.view(torch.float32)
+        bias = fl.as_strided((n, b), (hb // 4, 1), fl.storage_offset() + (offset + self.bias_off) // 4)
         return k, v, bias

@@ -15,38 +15,40 @@ def _init(rank: int, world: int, port: int) -> None:
     dist.init_process_group("gloo", rank=rank, world_size=world)
 
 
-def _pattern(edge, nbytes: int) -> torch.Tensor:
-    s, r = edge
-    return ((torch.arange(nbytes, dtype=torch.int64) * 7 + 31 * s + 131 * r) % 251).to(torch.uint8)
+def _pattern(unit, nbytes: int) -> torch.Tensor:
+    s, r, g = unit
+    return ((torch.arange(nbytes, dtype=torch.int64) * 7 + 31 * s + 131 * r + 17 * g) % 251).to(torch.uint8)
 
 
 def exchange_worker(rank: int, world: int, port: int, n_blocks: int, budgets, errq) -> None:
     """Fill the send/local buffers per DistPlan, exchange with the plan's
-    splits, check every incoming edge lands where recv_offsets says."""
+    splits, check every incoming (edge, KV head) unit lands where
+    recv_offsets says."""
     try:
         from dcc_kv_b200.dist_layer import DistPlan
         _init(rank, world, port)
-        plan = DistPlan(n_blocks, world, 512, 2, 16, budgets)
+        plan = DistPlan(n_blocks, world, 512, 2, 16, budgets,
+                        help_heads={7: 1, 6: 1, 5: 1} if world == n_blocks else None)
         send = torch.zeros(max(sum(plan.send_splits(rank)), 1), dtype=torch.uint8)
         local = torch.zeros(max(plan.bytes_ij[(rank, rank)], 1), dtype=torch.uint8)
         bufs = {"send": send, "local": local}
-        for e, (buf, off) in plan.send_offsets(rank).items():
-            n = plan.layout[e].nbytes
-            bufs[buf][off:off + n] = _pattern(e, n)
+        for u, (buf, off) in plan.send_offsets(rank).items():
+            n = plan.layout[(u[0], u[1])].head_bytes
+            bufs[buf][off:off + n] = _pattern(u, n)
         recv = torch.zeros(max(sum(plan.recv_splits(rank)), 1), dtype=torch.uint8)
         ss, rs = plan.send_splits(rank), plan.recv_splits(rank)
         dist.all_to_all_single(recv[:sum(rs)], send[:sum(ss)], output_split_sizes=rs, input_split_sizes=ss)
         bufs["recv"] = recv
-        for e, (buf, off) in plan.recv_offsets(rank).items():
-            n = plan.layout[e].nbytes
-            assert plan.consumer(e) == rank
-            if not torch.equal(bufs[buf][off:off + n], _pattern(e, n)):
-                raise AssertionError(f"rank {rank}: edge {e} wrong at {buf}+{off}")
+        for u, (buf, off) in plan.recv_offsets(rank).items():
+            n = plan.layout[(u[0], u[1])].head_bytes
+            assert plan.consumer(u) == rank
+            if not torch.equal(bufs[buf][off:off + n], _pattern(u, n)):
+                raise AssertionError(f"rank {rank}: unit {u} wrong at {buf}+{off}")
         # the compact-attention hand-off (one block per rank), in the layer's
         # order: helped blocks' queries to their helpers, then each helper's
         # partial state back to the helped block's rank
         mine = plan.local_blocks(rank)
-        helped = [r for r in mine if plan.help.get(r, 0) > 0]
+        helped = [r for r in mine if r in plan.help]
         helping = plan.helped_by(rank)
         q_in = {r: torch.zeros(64) for r in helping}
         ops = [dist.P2POp(dist.isend, torch.full((64,), float(r)), plan.helper(r)) for r in helped]

@@ -42,22 +42,32 @@ def _spawn(target, world, *args):
 
 @pytest.mark.parametrize("world", [1, 2, 4, 8])
 def test_plan_routes_every_edge_once(world):
+    """Every (edge, KV head) unit is written once on its source's rank and
+    read once on the rank that attends with it; the heads of one edge that
+    a rank reads are contiguous (one KV segment)."""
     budgets = {(s, r): [256, 512, 1024, 2048][(s * 3 + r) % 4] for r in range(8) for s in range(r)}
     plan = DistPlan(8, world, 16384, 8, 128, budgets)
+    units = {(s, r, g) for (s, r) in budgets for g in range(8)}
     sent, received = {}, {}
     for rank in range(world):
-        for e, loc in plan.send_offsets(rank).items():
-            assert plan.owner(e[0]) == rank and e not in sent
-            sent[e] = (rank, loc)
-        for e, loc in plan.recv_offsets(rank).items():
-            assert plan.consumer(e) == rank and e not in received
-            received[e] = (rank, loc)
+        for u, loc in plan.send_offsets(rank).items():
+            assert plan.owner(u[0]) == rank and u not in sent
+            sent[u] = (rank, loc)
+        recv = plan.recv_offsets(rank)
+        for u, loc in recv.items():
+            assert plan.consumer(u) == rank and u not in received
+            received[u] = (rank, loc)
         # byte ranges of one buffer never overlap
-        for offsets in (plan.send_offsets(rank), plan.recv_offsets(rank)):
-            spans = sorted((buf, off, off + plan.layout[e].nbytes) for e, (buf, off) in offsets.items())
+        for offsets in (plan.send_offsets(rank), recv):
+            spans = sorted((buf, off, off + plan.layout[(u[0], u[1])].head_bytes) for u, (buf, off) in offsets.items())
             for a, b in zip(spans, spans[1:]):
                 assert a[0] != b[0] or a[2] <= b[1]
-    assert set(sent) == set(received) == set(budgets)
+        for e in budgets:
+            lo, hi = plan.heads_on(rank, e)
+            for g in range(lo + 1, hi):
+                buf, off = recv[(e[0], e[1], g)]
+                assert recv[(e[0], e[1], g - 1)] == (buf, off - plan.layout[e].head_bytes)
+    assert set(sent) == set(received) == units
     for i in range(world):
         for j in range(world):
             assert plan.send_splits(i)[j] == plan.recv_splits(j)[i]
@@ -80,25 +90,27 @@ def test_snake_mapping_balances_compact_and_build_work(world):
     assert len({sum(7 - b for b in p) for p in parts}) == 1
 
 
-def test_plan_hands_sources_of_heavy_blocks_to_their_mirror():
-    """One block per rank: block r > its mirror 7 - r hands its first
-    (r - (7 - r)) // 2 compact sources to the mirror's rank, which caps the
-    compact attention per rank at 4 of the 7 blocks of the last one."""
+def test_plan_hands_kv_heads_of_heavy_blocks_to_their_mirror():
+    """One block per rank (the 128K layer on 8 GPUs): the cost model hands
+    the compact attention of the first 3 / 2 / 1 KV heads of blocks 7 / 6 /
+    5 to the ranks of their mirrors 0 / 1 / 2, which evens out the
+    estimated per-rank work (local attention, builds, compact attention and
+    the hand-off transfers)."""
     plan = DistPlan(8, 8, 16384, 8, 128, 1024)
     assert plan.help == {7: 3, 6: 2, 5: 1}
-    load = [0] * 8
-    for (s, r) in plan.budgets:
-        load[plan.consumer((s, r))] += 1
-    assert max(load) == 4 and sum(load) == 28
     assert plan.helped_by(0) == [7] and plan.helped_by(1) == [6] and plan.helped_by(7) == []
-    assert plan.consumer((2, 7)) == 0 and plan.consumer((3, 7)) == 7
+    assert plan.consumer((2, 7, 2)) == 0 and plan.consumer((2, 7, 3)) == 7
+    assert plan.heads_on(0, (4, 7)) == (0, 3) and plan.heads_on(7, (4, 7)) == (3, 8)
+    assert plan.heads_on(3, (4, 7)) == (0, 0)
     # several blocks per rank: no hand-off; a forced one is refused
     assert DistPlan(8, 4, 16384, 8, 128, 1024).help == {}
     with pytest.raises(ValueError):
-        DistPlan(8, 4, 16384, 8, 128, 1024, help_sources={7: 2})
+        DistPlan(8, 4, 16384, 8, 128, 1024, help_heads={7: 2})
+    with pytest.raises(ValueError):
+        DistPlan(8, 8, 16384, 8, 128, 1024, help_heads={7: 8})  # all heads: nothing left on the owner
     # a forced hand-off on two ranks (the 2-GPU test's setting)
-    plan2 = DistPlan(2, 2, 512, 2, 128, 64, help_sources={1: 1})
-    assert plan2.consumer((0, 1)) == 0 and plan2.helped_by(0) == [1]
+    plan2 = DistPlan(2, 2, 512, 2, 128, 64, help_heads={1: 1})
+    assert plan2.consumer((0, 1, 0)) == 0 and plan2.consumer((0, 1, 1)) == 1 and plan2.helped_by(0) == [1]
 
 
 def test_plan_rejects_uneven_split():
@@ -107,19 +119,28 @@ def test_plan_rejects_uneven_split():
 
 
 def test_edge_layout_alignment():
+    """KV-head-major blocks: every head starts 256-byte aligned, its keys,
+    values and bias 16-byte aligned, and a run of heads is one byte range."""
     for rows in (1, 45, 64, 1024):
         lay = EdgeLayout(3, rows, 128, 2)
-        assert lay.nbytes % 256 == 0
+        assert lay.head_bytes % 256 == 0 and lay.nbytes == 3 * lay.head_bytes
         assert lay.values_off % 16 == 0 and lay.bias_off % 16 == 0
         buf = torch.zeros(lay.nbytes * 2, dtype=torch.uint8)
         k, v, b = lay.views(buf, lay.nbytes, torch.bfloat16)
         assert k.shape == (3, rows, 128) and b.shape == (3, rows)
+        k[2].fill_(1.0)
+        v[1].fill_(2.0)
+        b[0].fill_(3.0)
+        k1, v1, b1 = lay.views(buf, lay.nbytes + lay.head_bytes, torch.bfloat16, n_heads=2)
+        assert torch.all(k1[1] == 1.0) and torch.all(v1[0] == 2.0) and torch.all(b1 == 0.0)
+        with pytest.raises(ValueError):
+            lay.views(buf, 128, torch.bfloat16)
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_gloo_exchange_by_plan(world):
-    """8 ranks: one block per rank, so the plan also hands compact sources of
-    blocks 5-7 to their mirrors' ranks (edge routing and the point-to-point
+    """8 ranks: one block per rank, so the plan also hands KV heads of
+    blocks 5-7 to their mirrors' ranks (unit routing and the point-to-point
     transfers of queries and partial states)."""
     budgets = {(s, r): [17, 64, 100][(s + r) % 3] for r in range(8) for s in range(r)}
     _spawn(dist_workers.exchange_worker, world, 8, budgets)

@@ -132,17 +132,17 @@ def _worker(rank, world, port, errq, nb):
 
 @pytest.mark.parametrize("world", [1, 2, 4])
 def test_distributed_layer_matches_oracle_and_single_gpu(world):
-    """4 blocks on 1, 2 or 4 ranks (4 ranks: one block per rank, so the
-    default hand-off {3: 1} is on)."""
+    """4 blocks on 1, 2 or 4 ranks (4 ranks: one block per rank; the cost
+    model hands nothing off at this small size)."""
     _spawn(_worker, world, NB)
 
 
-def test_distributed_layer_8_ranks_default_handoff():
-    """8 blocks on 8 ranks: the default hand-off {7: 3, 6: 2, 5: 1}."""
+def test_distributed_layer_8_ranks():
+    """8 blocks on 8 ranks (one block per rank)."""
     _spawn(_worker, 8, 8)
 
 
-def _stack_worker(rank, world, port, errq, nb, help_sources):
+def _stack_worker(rank, world, port, errq, nb, help_heads):
     try:
         dist, dev = _init(rank, world, port)
         from dcc_kv_b200.dist_layer import DistributedDccKvLayer, DistributedDccKvStack
@@ -154,9 +154,9 @@ def _stack_worker(rank, world, port, errq, nb, help_sources):
         for seed in (11, 29, 47):
             q, k, v = layer_inputs(nb, L, HQ, HKV, D, device="cpu", first_seed=seed)
             inputs.append(tuple(t[mine].contiguous().to(dev) for t in (q, k, v)))
-        kw = dict(window=128, device=dev, help_sources=help_sources)
+        kw = dict(window=128, device=dev, help_heads=help_heads)
         layer = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, **kw)
-        assert bool(layer.plan.help) == bool(help_sources)
+        assert bool(layer.plan.help) == bool(help_heads)
         want = [layer(*x).clone() for x in inputs]
         # no communication-computation overlap: same kernels, same outputs
         layer.overlap_exchange = False
@@ -176,12 +176,12 @@ def _stack_worker(rank, world, port, errq, nb, help_sources):
         errq.put(traceback.format_exc())
 
 
-@pytest.mark.parametrize("world,nb,help_sources", [(1, NB, None), (2, NB, None), (2, 2, {1: 1}),
+@pytest.mark.parametrize("world,nb,help_heads", [(1, NB, None), (2, NB, None), (2, 2, {1: 1}),
                                                    (4, NB, {3: 1})])
-def test_layer_stack_double_buffered_exchange_matches_layer_by_layer(world, nb, help_sources):
+def test_layer_stack_double_buffered_exchange_matches_layer_by_layer(world, nb, help_heads):
     """Two layer slots, each with its own exchange buffers, hand-off buffers,
-    point-to-point stream and communicator, interleaved layer by layer."""
-    _spawn(_stack_worker, world, nb, help_sources)
+    point-to-point stream and communicators, interleaved layer by layer."""
+    _spawn(_stack_worker, world, nb, help_heads)
 
 
 def _help_worker(rank, world, port, errq):
@@ -193,17 +193,18 @@ def _help_worker(rank, world, port, errq):
         from dcc_kv_b200.workloads import layer_inputs
         nb = world
         budgets = _budgets(nb)
-        help_sources = {1: 1} if world == 2 else None  # 4 / 8 ranks: the default hand-off
+        # HKV = 2: the helper attends with KV head 0 (query heads 0-3) of the helped blocks
+        help_heads = {2: {1: 1}, 4: {3: 1}, 8: {7: 1, 6: 1, 5: 1}}[world]
         q, k, v = layer_inputs(nb, L, HQ, HKV, D, device="cpu", first_seed=13)
         mine = local_blocks_of(nb, world, rank)
         xs = [t[mine].contiguous().to(dev) for t in (q, k, v)]
-        layer = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev, help_sources=help_sources)
+        layer = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev, help_heads=help_heads)
         assert layer.plan.help, "no hand-off configured"
         out = None
         for _ in range(2):
             out = layer(*xs)
         torch.cuda.synchronize()
-        plain = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev, help_sources={})
+        plain = DistributedDccKvLayer(nb, L, HQ, HKV, D, budgets, window=128, device=dev, help_heads={})
         out0 = plain(*xs)
         torch.cuda.synchronize()
         from gpu_util import assert_no_device_timeouts
