@@ -45,6 +45,31 @@ __device__ __forceinline__ double ordered_sum(const S* base, int64_t stride, int
   return s;
 }
 
+// out[k] = ordered_sum(base + e0 + k * step, stride, n) for k < 4 (0 for
+// entries at or past `count`): four independent sums, so 32 loads are in
+// flight per step instead of 8; each sum adds in the same order.
+template <typename S>
+__device__ __forceinline__ void ordered_sum4(const S* base, int64_t e0, int64_t step, int64_t count,
+                                             int64_t stride, int n, double* out) {
+  double s[4] = {0.0, 0.0, 0.0, 0.0};
+  for (int t0 = 0; t0 < n; t0 += 8) {
+    double v[4][8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int64_t e = e0 + k * step;
+        v[k][q] = (e < count && t0 + q < n) ? (double)base[e + (int64_t)(t0 + q) * stride] : 0.0;
+      }
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+#pragma unroll
+      for (int q = 0; q < 8; ++q) s[k] += v[k][q];
+  }
+#pragma unroll
+  for (int k = 0; k < 4; ++k) out[k] = s[k];
+}
+
 // 64 x 64 partial Gram of a [64][kLdG] shared tile: out[a][a2] = sum_b Z[a][b] Z[a2][b]
 // (thread owns rows ta + 16 i and columns tb + 16 j, i, j < 4; 256 threads).
 __device__ __forceinline__ void tile_gram(const double* zs, double* out) {
@@ -148,7 +173,8 @@ struct SolveSmem {
   double* vv;      // [64]
   double* res;     // [64]
   double* diag;    // [64]
-  double* colbuf;  // [128]
+  double* colbuf;  // [132]
+  double* rsum;    // [128] row sums of the exponentials, then their reciprocals
   double* ws;      // [64][dv + 1]
 };
 
@@ -169,17 +195,38 @@ __device__ __forceinline__ void beta_stage(const BuildDesc<Acc>& p, const BuildP
     if (a < M && p.out_mass) p.out_mass[a] = s;
   }
   if (!(p.stages & kStageBeta)) {
-    for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) p.wv[bb] = load_side<TIn>(p.in_beta, bb);
+    for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) p.wv[bb] = load_side<TIn>(p.in_beta, bb) / (double)M;
     __syncthreads();
     return;
   }
   __syncthreads();
   const double lb = prm.lambda_beta;
   if (M < Bp) {
-    for (int e = threadIdx.x; e < M * M; e += blockDim.x) {
-      const int a = e / M, a2 = e % M;
-      const double s = ordered_sum(p.gpart + a * 64 + a2, 4096, p.n_btiles);
-      gram[a * kLdG + a2] = s + (a == a2 ? lb : 0.0);
+    const int nt = blockDim.x;
+    for (int e0 = threadIdx.x; e0 < 64 * 64; e0 += 4 * nt) {
+      // four Gram entries per thread at once (32 loads in flight); entry e is
+      // (a, a2) = (e / 64, e % 64) of the 64 x 64 partials, summed over the
+      // tiles in tile order
+      double v[4][8], acc[4] = {0.0, 0.0, 0.0, 0.0};
+      for (int t0 = 0; t0 < p.n_btiles; t0 += 8) {
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {
+            const int e = e0 + k * nt;
+            const bool in = e < 4096 && (e >> 6) < M && (e & 63) < M && t0 + q < p.n_btiles;
+            v[k][q] = in ? p.gpart[(int64_t)(t0 + q) * 4096 + e] : 0.0;
+          }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int q = 0; q < 8; ++q) acc[k] += v[k][q];
+      }
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int e = e0 + k * nt, a = e >> 6, a2 = e & 63;
+        if (e < 4096 && a < M && a2 < M) gram[a * kLdG + a2] = acc[k] + (a == a2 ? lb : 0.0);
+      }
     }
     __syncthreads();
     chol64(gram, kLdG, M, sm.diag, sm.colbuf);
@@ -187,17 +234,29 @@ __device__ __forceinline__ void beta_stage(const BuildDesc<Acc>& p, const BuildP
     __syncthreads();
     if (threadIdx.x < 32) chol64_solve_vec(gram, kLdG, sm.diag, M, vv);
     __syncthreads();
-    for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) {
-      double w = 0.0;
+    // w = G^T v: four columns per thread at once (32 loads in flight)
+    for (int b0 = threadIdx.x; b0 < Bp; b0 += 4 * nt) {
+      double w[4] = {0.0, 0.0, 0.0, 0.0};
       for (int a0 = 0; a0 < M; a0 += 8) {
-        double g[8];
+        double g[4][8];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) g[q] = a0 + q < M ? p.G[(int64_t)(a0 + q) * Bp + bb] : 0.0;
+        for (int k = 0; k < 4; ++k)
 #pragma unroll
-        for (int q = 0; q < 8; ++q)
-          if (a0 + q < M) w = fma(g[q], vv[a0 + q], w);
+          for (int q = 0; q < 8; ++q) {
+            const int bb = b0 + k * nt;
+            g[k][q] = (a0 + q < M && bb < Bp) ? p.G[(int64_t)(a0 + q) * Bp + bb] : 0.0;
+          }
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+#pragma unroll
+          for (int q = 0; q < 8; ++q)
+            if (a0 + q < M) w[k] = fma(g[k][q], vv[a0 + q], w[k]);
       }
-      p.wv[bb] = w > 0.0 ? w : 0.0;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int bb = b0 + k * nt;
+        if (bb < Bp) p.wv[bb] = w[k] > 0.0 ? w[k] : 0.0;
+      }
     }
   } else {
     for (int e = threadIdx.x; e < M * Bp; e += blockDim.x) gsm[(e / Bp) * kLdG + e % Bp] = p.G[e];
@@ -235,7 +294,9 @@ __device__ __forceinline__ void beta_stage(const BuildDesc<Acc>& p, const BuildP
   __syncthreads();
   for (int bb = threadIdx.x; bb < Bp; bb += blockDim.x) {
     const double beta = log(fmax(p.wv[bb], 1e-6));
-    p.wv[bb] = beta;
+    // the value fit adds beta / M to every row of logits (value_regression.py:72-73):
+    // wv keeps that quotient from here on
+    p.wv[bb] = beta / (double)M;
     if (sizeof(TIn) == 8)
       static_cast<double*>(p.out_bias)[bb] = beta;
     else
@@ -245,70 +306,156 @@ __device__ __forceinline__ void beta_stage(const BuildDesc<Acc>& p, const BuildP
 }
 
 // ---- 3. X = softmax_b(logits + beta / M), one warp per row ------------------------------
+// Passes over the row (logits + beta / M and the max; exponentials and their
+// sum), each issuing eight independent loads per lane before it stores: the
+// row lives in L2, and a load-store chain per element would wait on every
+// access.  The row sums go to rsum; the division by them happens in
+// xgram_stage (M < B', where X is also needed in shared memory for X X^T)
+// or in a third pass here (B' <= M).
 template <typename Acc>
-__device__ __forceinline__ void x_stage(const BuildDesc<Acc>& p) {
+__device__ __forceinline__ void x_stage(const BuildDesc<Acc>& p, double* rsum) {
   const int Bp = cal_bp(p), M = p.M;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int a = warp; a < M; a += blockDim.x >> 5) {
-    double* xr = p.X + (int64_t)a * Bp;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
+  const double* __restrict__ bm = p.wv;  // beta / M
+  constexpr int kU = 8;
+  for (int a = warp; a < M; a += nwarps) {
+    double* __restrict__ xr = p.X + (int64_t)a * Bp;
     double mx = -INFINITY;
-    for (int bb = lane; bb < Bp; bb += 32) {
-      const double v = xr[bb] + p.wv[bb] / (double)M;  // value_regression.py:72-73
-      xr[bb] = v;
-      mx = fmax(mx, v);
+    for (int b0 = 0; b0 < Bp; b0 += 32 * kU) {
+      double v[kU];
+#pragma unroll
+      for (int q = 0; q < kU; ++q) {
+        const int bb = b0 + q * 32 + lane;
+        v[q] = bb < Bp ? xr[bb] + bm[bb] : -INFINITY;
+      }
+#pragma unroll
+      for (int q = 0; q < kU; ++q) {
+        const int bb = b0 + q * 32 + lane;
+        if (bb < Bp) xr[bb] = v[q];
+        mx = fmax(mx, v[q]);
+      }
     }
     mx = warp_max(mx);
     double sum = 0.0;
-    for (int bb = lane; bb < Bp; bb += 32) {
-      const double e = exp(xr[bb] - mx);
-      xr[bb] = e;
-      sum += e;
+    for (int b0 = 0; b0 < Bp; b0 += 32 * kU) {
+      double v[kU];
+#pragma unroll
+      for (int q = 0; q < kU; ++q) {
+        const int bb = b0 + q * 32 + lane;
+        v[q] = bb < Bp ? xr[bb] : -INFINITY;
+      }
+#pragma unroll
+      for (int q = 0; q < kU; ++q) {
+        const int bb = b0 + q * 32 + lane;
+        const double e = exp(v[q] - mx);
+        if (bb < Bp) {
+          xr[bb] = e;
+          sum += e;
+        }
+      }
     }
     sum = warp_sum(sum);
-    for (int bb = lane; bb < Bp; bb += 32) xr[bb] = xr[bb] / sum;
+    if (lane == 0) rsum[a] = sum;
+    if (M < Bp) continue;
+    for (int b0 = 0; b0 < Bp; b0 += 32 * kU) {
+      double v[kU];
+#pragma unroll
+      for (int q = 0; q < kU; ++q) {
+        const int bb = b0 + q * 32 + lane;
+        v[q] = bb < Bp ? xr[bb] : 0.0;
+      }
+#pragma unroll
+      for (int q = 0; q < kU; ++q) {
+        const int bb = b0 + q * 32 + lane;
+        if (bb < Bp) xr[bb] = v[q] / sum;
+      }
+    }
   }
   __syncthreads();
 }
 
-// ---- 4. X X^T + lam I over all 64-key tiles (M < B'), accumulated in tile order ---------
+// ---- 4. X = exponentials / row sums, tile by tile, and X X^T + lam I (M < B') -----------
+// Each 64-key tile of the exponentials is loaded once (16 loads per thread in
+// flight), scaled by the reciprocal row sums, stored as X (global, for C_V)
+// and into shared memory, and folded into the Gram.  The Gram is symmetric:
+// 252 threads each own one 8 x 8 block of its lower triangle (36 blocks) for
+// one of 7 groups of the tile's columns (c = g, g + 7, ...), 64 accumulators
+// in registers, so a thread reads 16 shared values per 64 FMAs; the 7 group
+// partials are added in group order at the end and mirrored to the upper
+// triangle.
 template <typename Acc>
-__device__ __forceinline__ void xgram_stage(const BuildDesc<Acc>& p, double lam, const SolveSmem& sm) {
+__device__ __forceinline__ void xgram_stage(const BuildDesc<Acc>& p, double lam, double* rsum,
+                                            const SolveSmem& sm) {
   const int Bp = cal_bp(p), M = p.M;
-  const int ta = threadIdx.x & 15, tb = threadIdx.x >> 4;
-  double acc[4][4];
+  constexpr int kGroups = 7, kBlocks = 36;
+  const int t = threadIdx.x;
+  const bool active = t < kGroups * kBlocks;
+  const int grp = t / kBlocks, blk = t % kBlocks;
+  int bi = 0;
+  while ((bi + 1) * (bi + 2) / 2 <= blk) ++bi;
+  const int bj = blk - bi * (bi + 1) / 2;
+  double acc[8][8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int u = 0; u < 8; ++u)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.0;
+    for (int v = 0; v < 8; ++v) acc[u][v] = 0.0;
+  if (t < 64) rsum[64 + t] = t < M ? 1.0 / rsum[t] : 0.0;  // reciprocal row sums
+  __syncthreads();
+  const double* inv = rsum + 64;
   double* xs = sm.gsm;
+  constexpr int kPer = 64 * kCalTile / 256;  // elements per thread per tile (blockDim.x == 256)
   for (int b0 = 0; b0 < Bp; b0 += kCalTile) {
-    for (int e = threadIdx.x; e < 64 * kCalTile; e += blockDim.x) {
-      const int a = e / kCalTile, bb = e % kCalTile;
-      xs[a * kLdG + bb] = (a < M && b0 + bb < Bp) ? p.X[(int64_t)a * Bp + b0 + bb] : 0.0;
+    double v[kPer];
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = t + i * 256, a = e / kCalTile, bb = e % kCalTile;
+      v[i] = (a < M && b0 + bb < Bp) ? p.X[(int64_t)a * Bp + b0 + bb] : 0.0;
+    }
+#pragma unroll
+    for (int i = 0; i < kPer; ++i) {
+      const int e = t + i * 256, a = e / kCalTile, bb = e % kCalTile;
+      const bool in = a < M && b0 + bb < Bp;
+      const double x = in ? v[i] * inv[a] : 0.0;
+      if (in) p.X[(int64_t)a * Bp + b0 + bb] = x;
+      xs[a * kLdG + bb] = x;
     }
     __syncthreads();
-#pragma unroll 4
-    for (int c = 0; c < kCalTile; ++c) {
-      double xa[4], xb[4];
+    if (active) {
+      for (int c = grp; c < kCalTile; c += kGroups) {
+        double xa[8], xb[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        xa[i] = xs[(ta + 16 * i) * kLdG + c];
-        xb[i] = xs[(tb + 16 * i) * kLdG + c];
+        for (int u = 0; u < 8; ++u) {
+          xa[u] = xs[(bi * 8 + u) * kLdG + c];
+          xb[u] = xs[(bj * 8 + u) * kLdG + c];
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u)
+#pragma unroll
+          for (int w = 0; w < 8; ++w) acc[u][w] = fma(xa[u], xb[w], acc[u][w]);
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fma(xa[i], xb[j], acc[i][j]);
     }
     __syncthreads();
   }
+  double* gram = sm.gram;
+  for (int g = 0; g < kGroups; ++g) {
+    if (active && grp == g) {
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+      for (int u = 0; u < 8; ++u)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int a = ta + 16 * i, a2 = tb + 16 * j;
-      if (a < M && a2 < M) sm.gram[a * kLdG + a2] = acc[i][j] + (a == a2 ? lam : 0.0);
+        for (int w = 0; w < 8; ++w) {
+          double* dst = gram + (bi * 8 + u) * kLdG + bj * 8 + w;
+          *dst = g == 0 ? acc[u][w] : *dst + acc[u][w];
+        }
     }
+    __syncthreads();
+  }
+  for (int e = t; e < 64 * 64; e += blockDim.x) {
+    const int a = e >> 6, a2 = e & 63;
+    if (a < M && a2 < M) {
+      if (a2 > a) gram[a * kLdG + a2] = gram[a2 * kLdG + a];
+      else if (a2 == a) gram[a * kLdG + a] += lam;
+    }
+  }
   __syncthreads();
 }
 
@@ -319,10 +466,17 @@ __device__ __forceinline__ void w_stage(const BuildDesc<Acc>& p, const BuildPara
   const int Bp = cal_bp(p), M = p.M, dv = prm.dv;
   double *gram = sm.gram, *gsm = sm.gsm, *ws = sm.ws;
   const int ldw = dv + 1;
-  for (int e = threadIdx.x; e < M * dv; e += blockDim.x) {  // Y, chunk order
-    const double s = ordered_sum(p.yp + e, (int64_t)M * dv, p.n_chunks);
-    p.Y[e] = s;
-    ws[(e / dv) * ldw + e % dv] = s;
+  for (int e0 = threadIdx.x; e0 < M * dv; e0 += 4 * blockDim.x) {  // Y, chunk order, 4 entries at once
+    double y[4];
+    ordered_sum4(p.yp, e0, blockDim.x, (int64_t)M * dv, (int64_t)M * dv, p.n_chunks, y);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = e0 + k * blockDim.x;
+      if (e < M * dv) {
+        p.Y[e] = y[k];
+        ws[(e / dv) * ldw + e % dv] = y[k];
+      }
+    }
   }
   const double lv = prm.lambda_value;
   // system size: M x M (push-through form) or B' x B' (literal form)
@@ -366,11 +520,12 @@ __global__ void __launch_bounds__(256) calib_solve_kernel(const __grid_constant_
   sm.res = sm.vv + 64;
   sm.diag = sm.res + 64;
   sm.colbuf = sm.diag + 64;
-  sm.ws = sm.colbuf + 128;
+  sm.rsum = sm.colbuf + 132;
+  sm.ws = sm.rsum + 128;
   beta_stage<TIn, Acc>(p, prm, sm);
   if (!(p.stages & kStageValues)) return;
-  x_stage(p);
-  if (p.M < cal_bp(p)) xgram_stage(p, prm.lambda_value, sm);
+  x_stage(p, sm.rsum);
+  if (p.M < cal_bp(p)) xgram_stage(p, prm.lambda_value, sm.rsum, sm);
   w_stage<TIn, Acc>(p, prm, sm);
 }
 
@@ -437,7 +592,7 @@ int launch_calibrate(const BuildBatch<Acc>& b, const BuildParams& prm, cudaStrea
   int tmax = 1;
   for (int i = 0; i < b.n; ++i) tmax = b.p[i].n_btiles > tmax ? b.p[i].n_btiles : tmax;
   const size_t smem1 = 3 * 64 * kLdG * sizeof(double);
-  const size_t smem2 = (2 * 64 * kLdG + 4 * 64 + 128 + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
+  const size_t smem2 = (2 * 64 * kLdG + 4 * 64 + 132 + 128 + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
   const size_t smem6 = (64 * kLdG + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
   auto k1 = calib_logits_kernel<TIn, Acc>;
   auto k2 = calib_solve_kernel<TIn, Acc>;

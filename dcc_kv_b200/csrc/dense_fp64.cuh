@@ -132,39 +132,57 @@ __device__ __forceinline__ void bar_sync_64() { asm volatile("bar.sync 2, 64;\n"
 // hold one row in registers as a window that shifts left by one column per
 // step (r[m] = A_i,k+m at step k), so every register index is static while
 // the step loop stays rolled (straight-line code of this size would be
-// instruction-fetch-bound: it runs once per CTA).  Step k publishes column k
-// through colbuf (2 x 64 doubles, alternating), takes one 64-thread barrier,
-// stores L_ik and applies A_ij -= A_ik A_jk / A_kk for k < j <= i.  Every
-// thread of the block calls it (it ends with __syncthreads()).
+// instruction-fetch-bound: it runs once per CTA).  Step k: one 64-thread
+// barrier, then L_ik = A_ik / sqrt(A_kk) and A_ij -= A_ik A_jk / A_kk for
+// k < j <= i, with 1 / sqrt(A_kk) and 1 / A_kk read from shared memory.
+// The step is pipelined: each row first updates the entry that becomes
+// column k + 1 and publishes it (colbuf, two alternating [66] buffers), and
+// the next pivot row computes the next step's two reciprocals right there,
+// so neither a division nor a square root sits between two barriers; the
+// other 62 updates of the row follow.  Every thread of the block calls it
+// (it ends with __syncthreads()).  colbuf: 132 doubles.
 __device__ __forceinline__ void chol64(double* A, int lda, int n, double* inv_diag, double* colbuf) {
   const int i = threadIdx.x;
   if (i < 64) {
     double r[64];
 #pragma unroll
     for (int m = 0; m < 64; ++m) r[m] = (i < n && m <= i) ? A[i * lda + m] : 0.0;
+    colbuf[i] = r[0];
+    if (i == 0) {
+      colbuf[64] = 1.0 / sqrt(r[0]);
+      colbuf[65] = 1.0 / r[0];
+    }
     for (int k = 0; k < n; ++k) {
-      double* col = colbuf + (k & 1) * 64;
-      col[i] = r[0];
+      const double* col = colbuf + (k & 1) * 66;
+      double* nxt = colbuf + ((k + 1) & 1) * 66;
       bar_sync_64();
-      const double d = col[k];
-      const double sd = sqrt(d);
+      const double isd = col[64], id = col[65];
       const bool below = i > k && i < n;
       if (i == k) {
-        A[i * lda + k] = sd;
-        inv_diag[k] = 1.0 / sd;
+        A[i * lda + k] = sqrt(r[0]);
+        inv_diag[k] = isd;
       } else if (below) {
-        A[i * lda + k] = r[0] / sd;
+        A[i * lda + k] = r[0] * isd;
       }
-      const double t = below ? r[0] / d : 0.0;
+      const double t = below ? r[0] * id : 0.0;
       const int span = below ? i - k : 0;  // columns k+1 .. i are updated
+      // the entry that becomes column k + 1, published for the next step
+      const double u1 = fma(-t, col[min(k + 1, 63)], r[1]);
+      const double n0 = 1 <= span ? u1 : r[1];
+      nxt[i] = n0;
+      if (i == k + 1 && i < n) {
+        nxt[64] = 1.0 / sqrt(n0);
+        nxt[65] = 1.0 / n0;
+      }
       // branch-free: every lane loads (clamped index, a broadcast) and
       // computes; the select keeps rows that are not updated unchanged
 #pragma unroll
-      for (int m = 1; m < 64; ++m) {
+      for (int m = 2; m < 64; ++m) {
         const double cj = col[min(k + m, 63)];
         const double u = fma(-t, cj, r[m]);
         r[m - 1] = m <= span ? u : r[m];
       }
+      r[0] = n0;
       r[63] = 0.0;
     }
     if (i < n)
@@ -173,42 +191,74 @@ __device__ __forceinline__ void chol64(double* A, int lda, int n, double* inv_di
   __syncthreads();
 }
 
-// Solve (L L^T) X = B in place for ncols <= blockDim.x right-hand sides, L
-// from chol64 (any n <= 64): column c of B at X[i * ldx + c], rows i < n.
-// One thread per column, substitution through shared memory with four
-// independent partial sums per row; L is read as warp-wide broadcasts.
+// Solve (L L^T) X = B in place for ncols <= 128 right-hand sides, L from
+// chol64 (any n <= 64): column c of B at X[i * ldx + c], rows i < n.
+// Blocked over 8-row panels with every thread of the block: per panel, the
+// 8 x 8 triangle is solved by one thread per column, then the rows below
+// (forward) or above (backward) are updated by a rank-8 product spread over
+// all threads, so only 2 x ceil(n / 8) short serial steps remain.
 __device__ __forceinline__ void chol64_solve(const double* L, int lda, const double* inv_diag, int n, double* X,
                                              int ldx, int ncols) {
-  const int c = threadIdx.x;
-  if (c < ncols) {
-    double* x = X + c;
-    for (int i = 0; i < n; ++i) {
-      const double* Li = L + i * lda;
-      double s0 = x[i * ldx], s1 = 0.0, s2 = 0.0, s3 = 0.0;
-      int j = 0;
-      for (; j + 4 <= i; j += 4) {
-        s0 = fma(-Li[j], x[j * ldx], s0);
-        s1 = fma(-Li[j + 1], x[(j + 1) * ldx], s1);
-        s2 = fma(-Li[j + 2], x[(j + 2) * ldx], s2);
-        s3 = fma(-Li[j + 3], x[(j + 3) * ldx], s3);
+  constexpr int kP = 8;
+  const int nt = blockDim.x;
+  // forward: L Y = B
+  for (int r0 = 0; r0 < n; r0 += kP) {
+    const int r1 = min(r0 + kP, n);
+    for (int c = threadIdx.x; c < ncols; c += nt) {
+      double y[kP];
+#pragma unroll
+      for (int q = 0; q < kP; ++q) {
+        const int i = r0 + q;
+        if (i < r1) {
+          double s = X[i * ldx + c];
+#pragma unroll
+          for (int j = 0; j < q; ++j) s = fma(-L[i * lda + r0 + j], y[j], s);
+          y[q] = s * inv_diag[i];
+          X[i * ldx + c] = y[q];
+        }
       }
-      for (; j < i; ++j) s0 = fma(-Li[j], x[j * ldx], s0);
-      x[i * ldx] = ((s0 + s1) + (s2 + s3)) * inv_diag[i];
     }
-    for (int i = n - 1; i >= 0; --i) {
-      double s0 = x[i * ldx], s1 = 0.0, s2 = 0.0, s3 = 0.0;
-      int j = i + 1;
-      for (; j + 4 <= n; j += 4) {
-        s0 = fma(-L[j * lda + i], x[j * ldx], s0);
-        s1 = fma(-L[(j + 1) * lda + i], x[(j + 1) * ldx], s1);
-        s2 = fma(-L[(j + 2) * lda + i], x[(j + 2) * ldx], s2);
-        s3 = fma(-L[(j + 3) * lda + i], x[(j + 3) * ldx], s3);
-      }
-      for (; j < n; ++j) s0 = fma(-L[j * lda + i], x[j * ldx], s0);
-      x[i * ldx] = ((s0 + s1) + (s2 + s3)) * inv_diag[i];
+    __syncthreads();
+    const int rows = n - r1;
+    for (int e = threadIdx.x; e < rows * ncols; e += nt) {
+      const int i = r1 + e / ncols, c = e % ncols;
+      double s = X[i * ldx + c];
+#pragma unroll
+      for (int j = 0; j < kP; ++j)
+        if (r0 + j < r1) s = fma(-L[i * lda + r0 + j], X[(r0 + j) * ldx + c], s);
+      X[i * ldx + c] = s;
     }
+    __syncthreads();
   }
-  __syncthreads();
+  // backward: L^T X = Y
+  for (int r1 = n; r1 > 0; r1 -= kP) {
+    const int r0 = max(r1 - kP, 0);
+    for (int c = threadIdx.x; c < ncols; c += nt) {
+      double x[kP];
+#pragma unroll
+      for (int q = kP - 1; q >= 0; --q) {
+        const int i = r0 + q;
+        if (i < r1) {
+          double s = X[i * ldx + c];
+#pragma unroll
+          for (int j = q + 1; j < kP; ++j)
+            if (r0 + j < r1) s = fma(-L[(r0 + j) * lda + i], x[j], s);
+          x[q] = s * inv_diag[i];
+          X[i * ldx + c] = x[q];
+        }
+      }
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < r0 * ncols; e += nt) {
+      const int i = e / ncols, c = e % ncols;
+      double s = X[i * ldx + c];
+#pragma unroll
+      for (int j = 0; j < kP; ++j)
+        if (r0 + j < r1) s = fma(-L[(r0 + j) * lda + i], X[(r0 + j) * ldx + c], s);
+      X[i * ldx + c] = s;
+    }
+    __syncthreads();
+  }
 }
 
 // Solve (L L^T) v = v in place for one right-hand side v[n] in shared
