@@ -34,11 +34,14 @@ class VarLenMessage:
 class DistributedComm:
     """comm.py:48-339 (backend gloo / nccl / mpi; mock mode without torch.distributed)."""
 
-    def __init__(self, backend: str = "gloo", mock: bool = False):
+    def __init__(self, backend: str = "gloo", mock: bool = False, group=None):
+        """``group`` (an addition to the reference's signature): the process
+        group every collective runs on; None is the default group."""
         if backend not in ("gloo", "nccl", "mpi"):
             raise ValueError(f"Unknown backend: {backend}; choose gloo/nccl/mpi")
         self.backend = backend
         self.mock = mock
+        self.group = group
         self.rank = 0
         self.world_size = 1
         self.initialized = False
@@ -52,9 +55,10 @@ class DistributedComm:
         if not self.mock:
             if not dist.is_initialized():
                 raise RuntimeError("torch.distributed not initialized; call setup_distributed() first")
-            if dist.get_rank() != rank or dist.get_world_size() != world_size:
+            g = self.group
+            if dist.get_rank(g) != rank or dist.get_world_size(g) != world_size:
                 raise ValueError(f"Comm init rank/ws mismatch: requested ({rank}/{world_size}), "
-                                 f"actual ({dist.get_rank()}/{dist.get_world_size()})")
+                                 f"actual ({dist.get_rank(g)}/{dist.get_world_size(g)})")
         self.initialized = True
 
     def cleanup(self) -> None:
@@ -89,14 +93,18 @@ class DistributedComm:
         recv = torch.empty((sum(recv_counts),) + tuple(send_tensor.shape[1:]), dtype=send_tensor.dtype,
                            device=send_tensor.device)
         dist.all_to_all_single(recv, send_tensor, output_split_sizes=list(recv_counts),
-                               input_split_sizes=list(send_counts))
+                               input_split_sizes=list(send_counts), group=self.group)
         return recv
 
     def all_to_all_v(self, messages: List[VarLenMessage], send_sizes: Optional[List[int]] = None,
                      recv_sizes: Optional[List[int]] = None, trust_recv_sizes: bool = False,
-                     out: Optional[torch.Tensor] = None) -> List[VarLenMessage]:
+                     out: Optional[torch.Tensor] = None,
+                     packed: Optional[torch.Tensor] = None) -> List[VarLenMessage]:
         """comm.py:174-280: variable-length all-to-all; ``out`` optionally
-        supplies the receive buffer [sum(recv_sizes), ...]."""
+        supplies the receive buffer [sum(recv_sizes), ...] and ``packed`` the
+        send buffer when the payloads already lie in it back to back (as
+        views, message i at offset sum(send_sizes[:i])), so no concatenation
+        copy is made."""
         self._check_init()
         if len(messages) != self.world_size:
             raise ValueError(f"messages length ({len(messages)}) != world_size ({self.world_size})")
@@ -121,12 +129,18 @@ class DistributedComm:
             st = torch.tensor(send_sizes, dtype=torch.long, device=first.device)
             rt = torch.empty_like(st)
             dist.all_to_all_single(rt, st, output_split_sizes=[1] * self.world_size,
-                                   input_split_sizes=[1] * self.world_size)
+                                   input_split_sizes=[1] * self.world_size, group=self.group)
             actual = rt.tolist()
-        send = torch.cat([m.payload for m in messages], dim=0)
+        if packed is not None:
+            if packed.shape[0] != sum(send_sizes):
+                raise ValueError(f"packed holds {packed.shape[0]} rows, send_sizes sum to {sum(send_sizes)}")
+            send = packed
+        else:
+            send = torch.cat([m.payload for m in messages], dim=0)
         recv = out if out is not None else torch.empty((sum(actual),) + tuple(first.shape[1:]), dtype=first.dtype,
                                                        device=first.device)
-        dist.all_to_all_single(recv, send, output_split_sizes=actual, input_split_sizes=list(send_sizes))
+        dist.all_to_all_single(recv, send, output_split_sizes=actual, input_split_sizes=list(send_sizes),
+                               group=self.group)
         res, off = [], 0
         for i, s in enumerate(actual):
             res.append(VarLenMessage(payload=recv[off:off + s], metadata={"src_rank": i, "size": s}))
@@ -137,19 +151,19 @@ class DistributedComm:
         self._check_init()
         if self.mock:
             return tensor.clone()
-        dist.all_reduce(tensor, op=op)
+        dist.all_reduce(tensor, op=op, group=self.group)
         return tensor
 
     def broadcast(self, tensor: torch.Tensor, src: int = 0) -> torch.Tensor:
         self._check_init()
         if self.mock:
             return tensor.clone()
-        dist.broadcast(tensor, src=src)
+        dist.broadcast(tensor, src=src, group=self.group)
         return tensor
 
     def barrier(self) -> None:
         if not self.mock and dist.is_initialized():
-            dist.barrier()
+            dist.barrier(group=self.group)
 
     def gather(self, tensor: torch.Tensor, dst: int = 0) -> Optional[List[torch.Tensor]]:
         self._check_init()
@@ -157,9 +171,9 @@ class DistributedComm:
             return [tensor.clone() for _ in range(self.world_size)]
         if self.rank == dst:
             out = [torch.empty_like(tensor) for _ in range(self.world_size)]
-            dist.gather(tensor, out, dst=dst)
+            dist.gather(tensor, out, dst=dst, group=self.group)
             return out
-        dist.gather(tensor, None, dst=dst)
+        dist.gather(tensor, None, dst=dst, group=self.group)
         return None
 
     def __repr__(self) -> str:

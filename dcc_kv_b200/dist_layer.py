@@ -15,6 +15,7 @@ blocks; round-robin would give 4 to 10).  One forward on every rank:
      per-destination-rank send buffer (edges between co-resident blocks go
      to a local buffer and never touch NCCL);
   2. exchange: one NCCL all-to-allv of the byte buffers on a side stream,
+     through ``DistributedComm.all_to_all_v`` (the reference's interface),
      sizes known from the shared budget table (no size round trip);
   3. local causal attention on the main stream from the start, overlapped
      with (0)-(2);
@@ -42,6 +43,7 @@ import torch.distributed as dist
 
 from . import _lib as L
 from .attention import attn_problem, kv_segment, run_attention
+from .comm import DistributedComm, VarLenMessage
 from .compact_kv import build_launch_count, build_problem, run_build_problems
 from .layer import Budgets, budget_table
 from .online_softmax import merge_lse
@@ -302,6 +304,14 @@ class DistributedDccKvLayer:
                 dist.barrier(group=self.p2p_group)
         if self.p2p_group is None:
             self.p2p_group = self.xgroup
+        # the exchange goes through the reference-interface wrapper
+        # (comm.py:174-280): sizes from the shared budget table (no size round
+        # trip), payloads already back to back in the send buffer, received
+        # in place
+        self.comm = DistributedComm(backend=dist.get_backend(self.xgroup), group=self.xgroup)
+        self.comm.init(self.rank, self.world)
+        offs = [sum(send_splits[:j]) for j in range(self.world)]
+        self._messages = [VarLenMessage(payload=self.send_buf[o:o + n]) for o, n in zip(offs, send_splits)]
         # pooling, the gather, the builds and the exchange run on a high-priority
         # side stream, so their kernels are dispatched ahead of the local
         # attention that fills the GPU meanwhile on the main stream
@@ -516,8 +526,8 @@ class DistributedDccKvLayer:
             run_build_problems(self.build, self.d, self.d, self.lb, self.lv, self.code, dev, self._ws)
             self._mark("builds", side)
             ns, nr = sum(self.send_splits), sum(self.recv_splits)
-            dist.all_to_all_single(self.recv_buf[:nr], self.send_buf[:ns], output_split_sizes=self.recv_splits,
-                                   input_split_sizes=self.send_splits, group=self.xgroup)
+            self.comm.all_to_all_v(self._messages, send_sizes=self.send_splits, recv_sizes=self.recv_splits,
+                                   trust_recv_sizes=True, out=self.recv_buf[:nr], packed=self.send_buf[:ns])
             self._mark("exchange", side)
         # helped blocks' queries to their helpers (after the collectives in
         # issue order, on a stream that waits only for the inputs)

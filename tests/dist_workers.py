@@ -90,6 +90,16 @@ def comm_worker(rank: int, world: int, port: int, errq) -> None:
                 assert m.metadata["src_rank"] == i
                 assert m.payload.shape == (recv_sizes[i], 3)
                 assert torch.all(m.payload == float(100 * i + rank))
+        # the layer's form: payloads as views of one packed send buffer, sizes
+        # trusted, received into a caller buffer
+        packed = torch.cat([m.payload for m in msgs])
+        offs = [sum(m.numel() for m in msgs[:j]) for j in range(world)]
+        views = [VarLenMessage(payload=packed[o:o + m.numel()]) for o, m in zip(offs, msgs)]
+        recv = torch.full((sum(recv_sizes), 3), -1.0)
+        out = comm.all_to_all_v(views, recv_sizes=recv_sizes, trust_recv_sizes=True, out=recv, packed=packed)
+        for i, m in enumerate(out):
+            assert m.payload.data_ptr() == recv[sum(recv_sizes[:i]):].data_ptr()
+            assert torch.all(m.payload == float(100 * i + rank))
         t = torch.tensor([float(rank + 1)])
         assert comm.all_reduce(t).item() == sum(range(1, world + 1))
         g = comm.gather(torch.tensor([rank]), dst=0)

@@ -2,8 +2,8 @@
 
 Run once in a container that holds the reference checkout (read-only):
 
-    python tests/golden/make_golden.py /root/reference             # everything
-    python tests/golden/make_golden.py /root/reference baselines   # baselines_small.npz only
+    python tests/golden/make_golden.py REFERENCE_CHECKOUT             # everything
+    python tests/golden/make_golden.py REFERENCE_CHECKOUT baselines   # baselines_small.npz only
 
 It imports ``src.dcc_kv_ref`` from that checkout, applies the FP64 dtype shim
 to ``rademacher_projection`` (the reference casts the projection to float32,
@@ -219,7 +219,9 @@ def baselines(root: str) -> None:
 
 
 if __name__ == "__main__":
-    root = sys.argv[1] if len(sys.argv) > 1 else "/root/reference"
+    if len(sys.argv) < 2:
+        sys.exit("usage: make_golden.py REFERENCE_CHECKOUT [baselines]")
+    root = sys.argv[1]
     if len(sys.argv) > 2 and sys.argv[2] == "baselines":
         baselines(root)
     else:
