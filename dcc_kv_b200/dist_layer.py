@@ -320,6 +320,11 @@ class DistributedDccKvLayer:
         # False: pooling, builds and exchange on the main stream before any
         # attention (no communication-computation overlap; same outputs)
         self.overlap_exchange = True
+        # True: the local attention waits for the pooling, which then runs on
+        # an idle GPU (its farthest-point-sampling clusters need several free
+        # SMs of one GPC at once; behind the attention CTAs they wait for
+        # them), so the gather, the builds and the exchange start sooner
+        self.pool_first = True
         self._bound = None
         self._bindings = {}
         self._host_stream = None
@@ -519,6 +524,10 @@ class DistributedDccKvLayer:
                 side.wait_event(windows_ready)
             select_query_sets(self.sets, self.d, self.M, self.dp, self.seed, self.code, dev)
             self._mark("pooling", side)
+            if self.pool_first and side is not main and self.sets:
+                pooled = torch.cuda.Event()
+                pooled.record(side)
+                main.wait_event(pooled)
             dist.all_gather_into_tensor(self.repr_all, self.repr_local, group=self.xgroup)
             self._mark("gather", side)
             if kv_ready is not None:
