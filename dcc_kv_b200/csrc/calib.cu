@@ -175,8 +175,28 @@ struct SolveSmem {
   double* diag;    // [64]
   double* colbuf;  // [132]
   double* rsum;    // [128] row sums of the exponentials, then their reciprocals
+  double* xt;      // [64 keys][kLdT] X tile, transposed, 2 doubles of padding per 8 rows
   double* ws;      // [64][dv + 1]
 };
+
+// Y = sum over the scoring chunks of the partial A V products, in chunk order,
+// into p.Y and the right-hand sides ws [M][dv + 1]; threads [t0, t0 + nt).
+template <typename Acc>
+__device__ __forceinline__ void y_sums(const BuildDesc<Acc>& p, int dv, double* ws, int tid, int nt) {
+  const int M = p.M, ldw = dv + 1;
+  for (int e0 = tid; e0 < M * dv; e0 += 4 * nt) {
+    double y[4];
+    ordered_sum4(p.yp, e0, nt, (int64_t)M * dv, (int64_t)M * dv, p.n_chunks, y);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int e = e0 + k * nt;
+      if (e < M * dv) {
+        p.Y[e] = y[k];
+        ws[(e / dv) * ldw + e % dv] = y[k];
+      }
+    }
+  }
+}
 
 template <typename TIn, typename Acc>
 __device__ __forceinline__ void beta_stage(const BuildDesc<Acc>& p, const BuildParams& prm, const SolveSmem& sm) {
@@ -229,7 +249,13 @@ __device__ __forceinline__ void beta_stage(const BuildDesc<Acc>& p, const BuildP
       }
     }
     __syncthreads();
-    chol64(gram, kLdG, M, sm.diag, sm.colbuf);
+    // the factorisation takes threads 0-63; the others sum Y (needed only by
+    // the value fit) meanwhile
+    if (threadIdx.x < 64)
+      chol64_rows(gram, kLdG, M, sm.diag, sm.colbuf);
+    else if (p.stages & kStageValues)
+      y_sums(p, prm.dv, sm.ws, threadIdx.x - 64, blockDim.x - 64);
+    __syncthreads();
     if (threadIdx.x < 64) vv[threadIdx.x] = tv[threadIdx.x];  // zero past M
     __syncthreads();
     if (threadIdx.x < 32) chol64_solve_vec(gram, kLdG, sm.diag, M, vv);
@@ -375,6 +401,7 @@ __device__ __forceinline__ void x_stage(const BuildDesc<Acc>& p, double* rsum) {
 }
 
 // ---- 4. X = exponentials / row sums, tile by tile, and X X^T + lam I (M < B') -----------
+constexpr int kLdT = 80;  // transposed X tile: 64 rows + 2 doubles of padding per 8
 // Each 64-key tile of the exponentials is loaded once (16 loads per thread in
 // flight), scaled by the reciprocal row sums, stored as X (global, for C_V)
 // and into shared memory, and folded into the Gram.  The Gram is symmetric:
@@ -402,7 +429,7 @@ __device__ __forceinline__ void xgram_stage(const BuildDesc<Acc>& p, double lam,
   if (t < 64) rsum[64 + t] = t < M ? 1.0 / rsum[t] : 0.0;  // reciprocal row sums
   __syncthreads();
   const double* inv = rsum + 64;
-  double* xs = sm.gsm;
+  double* xt = sm.xt;
   constexpr int kPer = 64 * kCalTile / 256;  // elements per thread per tile (blockDim.x == 256)
   for (int b0 = 0; b0 < Bp; b0 += kCalTile) {
     double v[kPer];
@@ -417,16 +444,23 @@ __device__ __forceinline__ void xgram_stage(const BuildDesc<Acc>& p, double lam,
       const bool in = a < M && b0 + bb < Bp;
       const double x = in ? v[i] * inv[a] : 0.0;
       if (in) p.X[(int64_t)a * Bp + b0 + bb] = x;
-      xs[a * kLdG + bb] = x;
+      xt[bb * kLdT + a + 2 * (a >> 3)] = x;
     }
     __syncthreads();
     if (active) {
       for (int c = grp; c < kCalTile; c += kGroups) {
+        // rows bi*8 .. bi*8+7 are 8 contiguous, 16-byte aligned doubles at
+        // bi * 10 (the padding spreads the 8 row blocks over distinct banks)
         double xa[8], xb[8];
+        const double2* ra = reinterpret_cast<const double2*>(xt + c * kLdT + bi * 10);
+        const double2* rb = reinterpret_cast<const double2*>(xt + c * kLdT + bj * 10);
 #pragma unroll
-        for (int u = 0; u < 8; ++u) {
-          xa[u] = xs[(bi * 8 + u) * kLdG + c];
-          xb[u] = xs[(bj * 8 + u) * kLdG + c];
+        for (int u = 0; u < 4; ++u) {
+          const double2 a2 = ra[u], b2 = rb[u];
+          xa[2 * u] = a2.x;
+          xa[2 * u + 1] = a2.y;
+          xb[2 * u] = b2.x;
+          xb[2 * u + 1] = b2.y;
         }
 #pragma unroll
         for (int u = 0; u < 8; ++u)
@@ -461,23 +495,14 @@ __device__ __forceinline__ void xgram_stage(const BuildDesc<Acc>& p, double lam,
 
 // ---- 5. Y, then W = (X X^T + lam I)^-1 Y   (B' <= M: C_V directly) ----------------------
 // For M < B' the Gram (with lam) is already in sm.gram.
+// y_done: Y is already in p.Y and ws (summed during the beta factorisation).
 template <typename TIn, typename Acc>
-__device__ __forceinline__ void w_stage(const BuildDesc<Acc>& p, const BuildParams& prm, const SolveSmem& sm) {
+__device__ __forceinline__ void w_stage(const BuildDesc<Acc>& p, const BuildParams& prm, const SolveSmem& sm,
+                                        bool y_done) {
   const int Bp = cal_bp(p), M = p.M, dv = prm.dv;
   double *gram = sm.gram, *gsm = sm.gsm, *ws = sm.ws;
   const int ldw = dv + 1;
-  for (int e0 = threadIdx.x; e0 < M * dv; e0 += 4 * blockDim.x) {  // Y, chunk order, 4 entries at once
-    double y[4];
-    ordered_sum4(p.yp, e0, blockDim.x, (int64_t)M * dv, (int64_t)M * dv, p.n_chunks, y);
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-      const int e = e0 + k * blockDim.x;
-      if (e < M * dv) {
-        p.Y[e] = y[k];
-        ws[(e / dv) * ldw + e % dv] = y[k];
-      }
-    }
-  }
+  if (!y_done) y_sums(p, dv, ws, threadIdx.x, blockDim.x);
   const double lv = prm.lambda_value;
   // system size: M x M (push-through form) or B' x B' (literal form)
   const int n = M < Bp ? M : Bp;
@@ -521,12 +546,14 @@ __global__ void __launch_bounds__(256) calib_solve_kernel(const __grid_constant_
   sm.diag = sm.res + 64;
   sm.colbuf = sm.diag + 64;
   sm.rsum = sm.colbuf + 132;
-  sm.ws = sm.rsum + 128;
+  sm.xt = sm.rsum + 128;
+  sm.ws = sm.xt + 64 * kLdT;
   beta_stage<TIn, Acc>(p, prm, sm);
   if (!(p.stages & kStageValues)) return;
   x_stage(p, sm.rsum);
   if (p.M < cal_bp(p)) xgram_stage(p, prm.lambda_value, sm.rsum, sm);
-  w_stage<TIn, Acc>(p, prm, sm);
+  // Y was summed during the beta factorisation on the push-through path
+  w_stage<TIn, Acc>(p, prm, sm, (p.stages & kStageBeta) && p.M < cal_bp(p));
 }
 
 // ---- 6. C_V = X^T W per 64-key tile --------------------------------------------------------
@@ -592,7 +619,7 @@ int launch_calibrate(const BuildBatch<Acc>& b, const BuildParams& prm, cudaStrea
   int tmax = 1;
   for (int i = 0; i < b.n; ++i) tmax = b.p[i].n_btiles > tmax ? b.p[i].n_btiles : tmax;
   const size_t smem1 = 3 * 64 * kLdG * sizeof(double);
-  const size_t smem2 = (2 * 64 * kLdG + 4 * 64 + 132 + 128 + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
+  const size_t smem2 = (2 * 64 * kLdG + 4 * 64 + 132 + 128 + 64 * kLdT + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
   const size_t smem6 = (64 * kLdG + 64 * (size_t)(prm.dv + 1)) * sizeof(double);
   auto k1 = calib_logits_kernel<TIn, Acc>;
   auto k2 = calib_solve_kernel<TIn, Acc>;

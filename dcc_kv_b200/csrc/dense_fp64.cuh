@@ -139,11 +139,20 @@ __device__ __forceinline__ void bar_sync_64() { asm volatile("bar.sync 2, 64;\n"
 // column k + 1 and publishes it (colbuf, two alternating [66] buffers), and
 // the next pivot row computes the next step's two reciprocals right there,
 // so neither a division nor a square root sits between two barriers; the
-// other 62 updates of the row follow.  Every thread of the block calls it
-// (it ends with __syncthreads()).  colbuf: 132 doubles.
+// other 62 updates of the row follow.  Every thread of the block calls
+// chol64 (it ends with __syncthreads()).  colbuf: 132 doubles.
+__device__ __forceinline__ void chol64_rows(double* A, int lda, int n, double* inv_diag, double* colbuf);
 __device__ __forceinline__ void chol64(double* A, int lda, int n, double* inv_diag, double* colbuf) {
+  if (threadIdx.x < 64) chol64_rows(A, lda, n, inv_diag, colbuf);
+  __syncthreads();
+}
+
+// The factorisation itself, run by threads 0-63 only (64-thread named
+// barrier): the other threads of the block may do independent work
+// meanwhile; the caller synchronises the block afterwards.
+__device__ __forceinline__ void chol64_rows(double* A, int lda, int n, double* inv_diag, double* colbuf) {
   const int i = threadIdx.x;
-  if (i < 64) {
+  {
     double r[64];
 #pragma unroll
     for (int m = 0; m < 64; ++m) r[m] = (i < n && m <= i) ? A[i * lda + m] : 0.0;
@@ -188,7 +197,6 @@ __device__ __forceinline__ void chol64(double* A, int lda, int n, double* inv_di
     if (i < n)
       for (int j = i + 1; j < n; ++j) A[i * lda + j] = 0.0;
   }
-  __syncthreads();
 }
 
 // Solve (L L^T) X = B in place for ncols <= 128 right-hand sides, L from
