@@ -548,6 +548,7 @@ def run_gpu(args, wl: LayerWorkload):
         kflops = n_local * HQ * (L * (L + 1) // 2) * 4 * D
         kname = f"local causal attention ({n_local} block(s) per GPU, one launch, rank 0)"
     achieved = kflops / (a_ms * 1e-3) / 1e12
+    layer_flops = sum(causal_attention_flops(wl))
     line = {
         "metric": wl.metric, "value": wl.tokens / (ms * 1e-3), "unit": "tokens/s", "n_gpus": ws,
         "steps": args.steps, "warmup": warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
@@ -565,6 +566,12 @@ def run_gpu(args, wl: LayerWorkload):
                      "algorithmic_bytes": alg_bytes,
                      "algorithmic_flops": kflops, "launches": a_launches,
                      "ms_per_launch": a_ms / max(a_launches, 1), "ms_per_step": a_ms},
+        # the whole layer against the whole job's tensor peak: every block's
+        # attention FLOPs (local + compact, the bulk of the layer's work) over
+        # n_gpus x the measured sustained peak x the step time
+        "layer_roofline": {"flops": layer_flops, "achieved": layer_flops / (ms * 1e-3) / 1e12,
+                           "peak": ws * tf_sust, "unit": "TFLOP/s",
+                           "frac": layer_flops / (ms * 1e-3) / 1e12 / (ws * tf_sust)},
         "clocks": clocks,
     }
     if args.cpu_baseline and ws == 1:
