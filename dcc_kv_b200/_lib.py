@@ -176,11 +176,13 @@ class DeviceErrorWatch:
     """Bounded device-side waits that gave up, seen from the host without a
     synchronisation.  The tcgen05 kernels never hang: a wait that passes its
     limit records a flag and the kernel unwinds, leaving its outputs
-    unusable.  ``record`` enqueues an asynchronous copy of the library's two
-    flags (attention, scoring) into a pinned host pair at the end of a
-    forward; ``poll`` raises ``DccError(DCC_ERR_TIMEOUT)`` when the copy
-    that has landed shows a flag, so a forward whose kernel gave up is
-    reported by the next call.  ``check`` synchronises the device first."""
+    unusable.  ``record`` enqueues one tiny kernel that writes the library's
+    two flags (attention, scoring) into a pinned host pair at the end of a
+    forward; ``poll`` raises ``DccError(DCC_ERR_TIMEOUT)`` when the pair, as
+    last written, shows a flag, so a forward whose kernel gave up is reported
+    by the next call.  ``check`` synchronises the device first.  The flags
+    belong to the device: a wait that gave up in any of the library's
+    kernels on it is reported, whichever layer launched it."""
 
     def __init__(self):
         self.host: Optional[torch.Tensor] = None
