@@ -870,7 +870,8 @@ def phase_study(args):
     q, k, v = (torch.stack([p_[i] for p_ in parts]) for i in range(3))
     del parts
     layer = DistributedDccKvLayer(wl.blocks, wl.block_len, HQ, HKV, D, wl.budgets, WINDOW, M_REPR, DP, device=dev)
-    layer.pool_first = args.pool_first
+    if args.pool_first is not None:
+        layer.pool_first = args.pool_first
     for _ in range(max(args.warmup, 3)):
         layer(q, k, v)
     _barrier(ws)
@@ -884,7 +885,7 @@ def phase_study(args):
     everyone = [None] * ws
     dist.all_gather_object(everyone, mine)
     if rank == 0:
-        print(json.dumps({"study": "phase times", "n_gpus": ws, "steps": args.steps, "pool_first": args.pool_first,
+        print(json.dumps({"study": "phase times", "n_gpus": ws, "steps": args.steps, "pool_first": layer.pool_first,
                           "config": wl.config(parallelism=f"context parallel over {ws} GPUs"),
                           "ranks": everyone}), flush=True)
     del layer
@@ -910,6 +911,9 @@ def main():
                     help="under torchrun, N >= 2: time the compact exchange synchronous, overlapped, and "
                          "double buffered across --layers layers, and exit")
     ap.add_argument("--layers", type=int, default=4, help="layers in a row for --exchange-study")
+    ap.add_argument("--pool-first", dest="pool_first", action="store_true", default=None,
+                    help="--phase-times: the local attention waits for the pooling (default: only with one "
+                         "block per rank)")
     ap.add_argument("--no-pool-first", dest="pool_first", action="store_false",
                     help="--phase-times: let the local attention start before the pooling finishes")
     ap.add_argument("--phase-times", action="store_true",

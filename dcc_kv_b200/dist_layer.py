@@ -323,8 +323,11 @@ class DistributedDccKvLayer:
         # True: the local attention waits for the pooling, which then runs on
         # an idle GPU (its farthest-point-sampling clusters need several free
         # SMs of one GPC at once; behind the attention CTAs they wait for
-        # them), so the gather, the builds and the exchange start sooner
-        self.pool_first = True
+        # them), so the gather, the builds and the exchange start sooner.  On
+        # by default with one block per rank, where the exchange is on the
+        # critical path; with several blocks per rank the local attention is
+        # long enough to hide it, and the wait would only delay the attention
+        self.pool_first = self.n_local == 1
         self._bound = None
         self._bindings = {}
         self._host_stream = None
