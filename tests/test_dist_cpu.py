@@ -108,10 +108,10 @@ def test_plan_hands_kv_heads_of_heavy_blocks_to_their_mirror():
         DistPlan(8, 4, 16384, 8, 128, 1024, help_heads={7: 2})
     with pytest.raises(ValueError):
         DistPlan(8, 8, 16384, 8, 128, 1024, help_heads={7: 8})  # all heads: nothing left on the owner
-    # the 1M layer (variable budgets): blocks 7 and 6 only; a small layer: none (the transfers
-    # would cost more than they save)
+    # the 1M layer (variable budgets): block 7 only; a small layer: none (the transfers would
+    # cost more than they save)
     from dcc_kv_b200.workloads import variable_budgets
-    assert DistPlan(8, 8, 131072, 8, 128, variable_budgets(8)).help == {7: 3, 6: 2}
+    assert DistPlan(8, 8, 131072, 8, 128, variable_budgets(8)).help == {7: 3}
     assert DistPlan(4, 4, 512, 2, 128, 96).help == {}
     # a forced hand-off on two ranks (the 2-GPU test's setting)
     plan2 = DistPlan(2, 2, 512, 2, 128, 64, help_heads={1: 1})
