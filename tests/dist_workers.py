@@ -100,7 +100,15 @@ def comm_worker(rank: int, world: int, port: int, errq) -> None:
         for i, m in enumerate(out):
             assert m.payload.data_ptr() == recv[sum(recv_sizes[:i]):].data_ptr()
             assert torch.all(m.payload == float(100 * i + rank))
+        # the same exchange on an explicit process group (the layer passes its own)
+        sub = dist.new_group(ranks=list(range(world)))
+        gcomm = DistributedComm(backend="gloo", group=sub)
+        gcomm.init(rank, world)
+        out = gcomm.all_to_all_v(msgs, recv_sizes=recv_sizes, trust_recv_sizes=True)
+        for i, m in enumerate(out):
+            assert torch.all(m.payload == float(100 * i + rank))
         t = torch.tensor([float(rank + 1)])
+        assert gcomm.all_reduce(t.clone()).item() == sum(range(1, world + 1))
         assert comm.all_reduce(t).item() == sum(range(1, world + 1))
         g = comm.gather(torch.tensor([rank]), dst=0)
         if rank == 0:
